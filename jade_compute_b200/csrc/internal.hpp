@@ -1,0 +1,77 @@
+// Runtime internals shared by the C ABI (runtime.cpp) and the kernel families.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "ir.hpp"
+
+namespace jade {
+
+struct Allocation {
+    size_t bytes;
+    bool host;  // pinned host memory (copy-job endpoints)
+};
+
+struct Context {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t start = nullptr, stop = nullptr;
+    std::map<uintptr_t, Allocation> allocations;
+    int *err_host = nullptr;  // mapped, written by kernels (first error wins)
+    int *err_dev = nullptr;
+    std::vector<cudaEvent_t> job_events;
+    // NCCL (opaque; see comm.cpp)
+    void *nccl_comm = nullptr;
+    int nranks = 1, rank = 0;
+    uint32_t comm_timeout_ms = 60000;
+    // cuBLAS handle for the gemm_mps library comparator (lazy)
+    void *cublas = nullptr;
+    // runtime-compiled elementwise modules, keyed by full source text
+    std::map<std::string, std::pair<void *, void *>> rtc_modules;  // source -> (CUmodule, CUfunction)
+    std::mutex rtc_mutex;
+};
+
+using LaunchFn = std::function<cudaError_t(cudaStream_t, void **)>;
+
+}  // namespace jade
+
+struct jr_kernel {
+    jade::Context *ctx = nullptr;
+    jade::Spec spec;
+    std::vector<jade::Binding> binds;
+    std::string impl;  // implementation name reported by jr_kernel_info
+    std::string path;  // "tcgen05", "simt", "nvrtc", "nccl", "copy", "cublas"
+    bool collective = false;
+    jade::LaunchFn run;
+};
+
+namespace jade {
+
+// Kernel families. Each returns a launch closure for the validated spec, or
+// throws IrError when the spec has no implementation on this backend.
+LaunchFn make_row_kernel(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_gemm_simt(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_gemm_tc(Context *ctx, const Spec &s, std::string &impl);  // tcgen05 path
+bool gemm_tc_supports(const Spec &s, std::string &why);
+LaunchFn make_attention_simt(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_attention_tc(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_elementwise_rtc(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl);  // fill, l2_flush
+LaunchFn make_cublas_gemm(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_all_reduce(Context *ctx, const Spec &s, std::string &impl);
+void cublas_destroy(Context *ctx);
+void rtc_destroy(Context *ctx);
+void comm_destroy(Context *ctx);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+void *driver_entry(const char *name);
+
+}  // namespace jade

@@ -1,0 +1,420 @@
+// HBM-bound kernels: axpy, add, SwiGLU (elementwise), RMSNorm, softmax and the
+// per-row inverse RMS used by the fused MLP (row kernels), plus fill and L2 flush.
+//
+// Reference semantics: src/runtime/ir.rs:485-523 (emitted bodies) and the FP64
+// oracles src/runtime/workloads.rs:36-55,134-141. Design for B200: 128-bit
+// loads/stores with streaming cache hints, grid sized to a multiple of the SM
+// count, and single-pass row kernels that keep the row in registers so x is read
+// from HBM exactly once (the reference reads it 2-3 times).
+#include <cfloat>
+
+#include "common.cuh"
+#include "internal.hpp"
+
+namespace jade {
+namespace {
+
+constexpr int kThreads = 256;
+
+int grid_for(const Context *ctx, uint64_t work, int per_block, int blocks_per_sm = 8) {
+    uint64_t need = (work + per_block - 1) / per_block;
+    uint64_t cap = (uint64_t)ctx->sm_count * blocks_per_sm;
+    if (need < 1) need = 1;
+    return (int)(need < cap ? need : cap);
+}
+
+// ------------------------------------------------------------------ axpy / add
+// out = fmaf(alpha, a, b): one correctly rounded FMA, bit-identical to ir.rs:485.
+__global__ void __launch_bounds__(kThreads) axpy_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                                                        float *__restrict__ out, float alpha, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t nv = n >> 2;
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+        const float4 x = __ldcs(reinterpret_cast<const float4 *>(a) + v);
+        const float4 y = __ldcs(reinterpret_cast<const float4 *>(b) + v);
+        float4 r;
+        r.x = fmaf(alpha, x.x, y.x);
+        r.y = fmaf(alpha, x.y, y.y);
+        r.z = fmaf(alpha, x.z, y.z);
+        r.w = fmaf(alpha, x.w, y.w);
+        __stcs(reinterpret_cast<float4 *>(out) + v, r);
+    }
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < (n & 3)) {
+        const uint64_t i = (nv << 2) + t;
+        out[i] = fmaf(alpha, a[i], b[i]);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) add_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                                                       float *__restrict__ out, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t nv = n >> 2;
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+        const float4 x = __ldcs(reinterpret_cast<const float4 *>(a) + v);
+        const float4 y = __ldcs(reinterpret_cast<const float4 *>(b) + v);
+        float4 r;
+        r.x = __fadd_rn(x.x, y.x);
+        r.y = __fadd_rn(x.y, y.y);
+        r.z = __fadd_rn(x.z, y.z);
+        r.w = __fadd_rn(x.w, y.w);
+        __stcs(reinterpret_cast<float4 *>(out) + v, r);
+    }
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < (n & 3)) {
+        const uint64_t i = (nv << 2) + t;
+        out[i] = __fadd_rn(a[i], b[i]);
+    }
+}
+
+// ------------------------------------------------------------------ SwiGLU
+// out = (v * sigmoid(v)) * up with the stable branch of ir.rs:487, same operation
+// order (expf, IEEE division), so FP32 results match the emitted reference kernel.
+__device__ __forceinline__ float swiglu1(float v, float u) { return (v * stable_sigmoid(v)) * u; }
+
+__global__ void __launch_bounds__(kThreads) swiglu_f32_kernel(const float *__restrict__ g, const float *__restrict__ up,
+                                                              float *__restrict__ out, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t nv = n >> 2;
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+        const float4 x = __ldcs(reinterpret_cast<const float4 *>(g) + v);
+        const float4 y = __ldcs(reinterpret_cast<const float4 *>(up) + v);
+        float4 r;
+        r.x = swiglu1(x.x, y.x);
+        r.y = swiglu1(x.y, y.y);
+        r.z = swiglu1(x.z, y.z);
+        r.w = swiglu1(x.w, y.w);
+        __stcs(reinterpret_cast<float4 *>(out) + v, r);
+    }
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < (n & 3)) {
+        const uint64_t i = (nv << 2) + t;
+        out[i] = swiglu1(g[i], up[i]);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const __nv_bfloat16 *__restrict__ g, const __nv_bfloat16 *__restrict__ up,
+                                                               __nv_bfloat16 *__restrict__ out, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t nv = n >> 3;  // 8 bf16 per 16 B
+    for (uint64_t v = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+        const uint4 x = __ldcs(reinterpret_cast<const uint4 *>(g) + v);
+        const uint4 y = __ldcs(reinterpret_cast<const uint4 *>(up) + v);
+        const __nv_bfloat162 *xa = reinterpret_cast<const __nv_bfloat162 *>(&x);
+        const __nv_bfloat162 *ya = reinterpret_cast<const __nv_bfloat162 *>(&y);
+        uint4 r;
+        uint32_t *ra = reinterpret_cast<uint32_t *>(&r);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 a2 = __bfloat1622float2(xa[q]), b2 = __bfloat1622float2(ya[q]);
+            ra[q] = pack_bf16(swiglu1(a2.x, b2.x), swiglu1(a2.y, b2.y));
+        }
+        __stcs(reinterpret_cast<uint4 *>(out) + v, r);
+    }
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < (n & 7)) {
+        const uint64_t i = (nv << 3) + t;
+        out[i] = __float2bfloat16_rn(swiglu1(__bfloat162float(g[i]), __bfloat162float(up[i])));
+    }
+}
+
+// ------------------------------------------------------------------ block reductions
+template <bool kMax>
+__device__ __forceinline__ float warp_reduce(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = kMax ? fmaxf(v, w) : v + w;
+    }
+    return v;
+}
+template <bool kMax>
+__device__ __forceinline__ float block_reduce(float v, float *scratch /* >= 32 floats */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_reduce<kMax>(v);
+    __syncthreads();  // scratch may still be read from a previous reduction
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float r = lane < nw ? scratch[lane] : (kMax ? -INFINITY : 0.0f);
+    return warp_reduce<kMax>(r);
+}
+
+// Loads/stores of 16-byte vectors of T (4 fp32 or 8 bf16) as float arrays.
+template <typename T> struct Vec;
+template <> struct Vec<float> {
+    static constexpr int N = 4;
+    __device__ static void load(const float *p, float *d) {
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(p));
+        d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+    }
+    __device__ static void load_keep(const float *p, float *d) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(p));
+        d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+    }
+    __device__ static void store(float *p, const float *d) {
+        __stcs(reinterpret_cast<float4 *>(p), make_float4(d[0], d[1], d[2], d[3]));
+    }
+};
+template <> struct Vec<__nv_bfloat16> {
+    static constexpr int N = 8;
+    __device__ static void unpack(uint4 v, float *d) {
+        const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { const float2 f = __bfloat1622float2(h[q]); d[2 * q] = f.x; d[2 * q + 1] = f.y; }
+    }
+    __device__ static void load(const __nv_bfloat16 *p, float *d) { unpack(__ldcs(reinterpret_cast<const uint4 *>(p)), d); }
+    __device__ static void load_keep(const __nv_bfloat16 *p, float *d) { unpack(__ldg(reinterpret_cast<const uint4 *>(p)), d); }
+    __device__ static void store(__nv_bfloat16 *p, const float *d) {
+        uint4 v;
+        uint32_t *a = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) a[q] = pack_bf16(d[2 * q], d[2 * q + 1]);
+        __stcs(reinterpret_cast<uint4 *>(p), v);
+    }
+};
+
+// Row kernels, register-resident: one block per row (grid-stride over rows),
+// each thread holds NV vectors. Requires cols % Vec::N == 0 and cols <= NV*N*blockDim.
+enum class RowOp { RmsNorm, Softmax, RmsInv };
+
+template <typename T, int NV, RowOp OP>
+__global__ void __launch_bounds__(kThreads) row_kernel(const T *__restrict__ x, const T *__restrict__ w, void *__restrict__ out_,
+                                                       uint32_t rows, uint32_t cols, float eps) {
+    __shared__ float scratch[32];
+    constexpr int N = Vec<T>::N;
+    const uint32_t nvec = cols / N;
+    for (uint32_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const T *xr = x + (uint64_t)row * cols;
+        float v[NV][N];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const uint32_t c = threadIdx.x + j * blockDim.x;
+            if (c < nvec) Vec<T>::load(xr + (uint64_t)c * N, v[j]);
+        }
+        if constexpr (OP == RowOp::Softmax) {
+            float m = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (threadIdx.x + j * blockDim.x < nvec)
+#pragma unroll
+                    for (int e = 0; e < N; ++e) m = fmaxf(m, v[j][e]);
+            m = block_reduce<true>(m, scratch);
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (threadIdx.x + j * blockDim.x < nvec)
+#pragma unroll
+                    for (int e = 0; e < N; ++e) { v[j][e] = expf(v[j][e] - m); s += v[j][e]; }
+            s = block_reduce<false>(s, scratch);
+            const float inv = 1.0f / s;
+            T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const uint32_t c = threadIdx.x + j * blockDim.x;
+                if (c < nvec) {
+#pragma unroll
+                    for (int e = 0; e < N; ++e) v[j][e] *= inv;
+                    Vec<T>::store(o + (uint64_t)c * N, v[j]);
+                }
+            }
+        } else {
+            float ss = 0.0f;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (threadIdx.x + j * blockDim.x < nvec)
+#pragma unroll
+                    for (int e = 0; e < N; ++e) ss = fmaf(v[j][e], v[j][e], ss);
+            ss = block_reduce<false>(ss, scratch);
+            const float inv = 1.0f / sqrtf(ss / (float)cols + eps);
+            if constexpr (OP == RowOp::RmsInv) {
+                if (threadIdx.x == 0) static_cast<float *>(out_)[row] = inv;
+            } else {
+                T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    const uint32_t c = threadIdx.x + j * blockDim.x;
+                    if (c < nvec) {
+                        float wv[N];
+                        Vec<T>::load_keep(w + (uint64_t)c * N, wv);
+#pragma unroll
+                        for (int e = 0; e < N; ++e) v[j][e] = v[j][e] * inv * wv[e];
+                        Vec<T>::store(o + (uint64_t)c * N, v[j]);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// General fallback for any cols (ragged or very wide rows): three passes over the
+// row through L2, one block per row, scalar accesses.
+template <typename T, RowOp OP>
+__global__ void __launch_bounds__(kThreads) row_kernel_general(const T *__restrict__ x, const T *__restrict__ w, void *__restrict__ out_,
+                                                               uint32_t rows, uint32_t cols, float eps) {
+    __shared__ float scratch[32];
+    for (uint32_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const T *xr = x + (uint64_t)row * cols;
+        if constexpr (OP == RowOp::Softmax) {
+            float m = -INFINITY;
+            for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, to_f32(xr[c]));
+            m = block_reduce<true>(m, scratch);
+            float s = 0.0f;
+            for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) s += expf(to_f32(xr[c]) - m);
+            s = block_reduce<false>(s, scratch);
+            const float inv = 1.0f / s;
+            T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
+            for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) o[c] = from_f32<T>(expf(to_f32(xr[c]) - m) * inv);
+        } else {
+            float ss = 0.0f;
+            for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) { const float v = to_f32(xr[c]); ss = fmaf(v, v, ss); }
+            ss = block_reduce<false>(ss, scratch);
+            const float inv = 1.0f / sqrtf(ss / (float)cols + eps);
+            if constexpr (OP == RowOp::RmsInv) {
+                if (threadIdx.x == 0) static_cast<float *>(out_)[row] = inv;
+            } else {
+                T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
+                for (uint32_t c = threadIdx.x; c < cols; c += blockDim.x) o[c] = from_f32<T>(to_f32(xr[c]) * inv * to_f32(w[c]));
+            }
+        }
+    }
+}
+
+template <typename T, RowOp OP>
+LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
+    constexpr int N = Vec<T>::N;
+    const uint32_t rows = s.rows, cols = s.cols;
+    const float eps = s.epsilon;
+    const int grid = grid_for(ctx, rows, 1, 16);
+    const bool vec = cols % N == 0;
+    const uint32_t per_thread = (cols / N + kThreads - 1) / kThreads;  // vectors per thread
+    using KFn = void (*)(const T *, const T *, void *, uint32_t, uint32_t, float);
+    KFn fn = nullptr;
+    if (vec && per_thread <= 1) fn = row_kernel<T, 1, OP>;
+    else if (vec && per_thread <= 2) fn = row_kernel<T, 2, OP>;
+    else if (vec && per_thread <= 4) fn = row_kernel<T, 4, OP>;
+    else if (vec && per_thread <= 8) fn = row_kernel<T, 8, OP>;
+    else if (vec && per_thread <= 16) fn = row_kernel<T, 16, OP>;
+    else fn = row_kernel_general<T, OP>;
+    impl = std::string(fn == (KFn)row_kernel_general<T, OP> ? "row_general_" : "row_register_") + dtype_name(s.dtype);
+    return [=](cudaStream_t st, void **b) {
+        const T *x = static_cast<const T *>(b[0]);
+        const T *w = OP == RowOp::RmsNorm ? static_cast<const T *>(b[1]) : nullptr;
+        void *out = OP == RowOp::RmsNorm ? b[2] : b[1];
+        fn<<<grid, kThreads, 0, st>>>(x, w, out, rows, cols, eps);
+        return cudaGetLastError();
+    };
+}
+
+// ------------------------------------------------------------------ fill / flush
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+// Counter-based synthetic inputs: element i of stream s from seed is
+// splitmix64(seed ^ s*C ^ i); uniform in [lo, hi) or normal (Box-Muller) with
+// mean lo and standard deviation hi; rounded once to the output type.
+template <typename T>
+__global__ void fill_kernel(T *__restrict__ out, uint64_t n, uint64_t seed, uint32_t stream, int normal, float lo, float hi) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t key = splitmix64(seed ^ (0xD1B54A32D192ED03ull * (uint64_t)(stream + 1)));
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t h = splitmix64(key + i);
+        float v;
+        if (normal) {
+            const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);            // (0,1)
+            const float u2 = (float)((h >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);     // [0,1)
+            v = lo + hi * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        } else {
+            const float u = (float)(h >> 40) * (1.0f / 16777216.0f);
+            v = lo + (hi - lo) * u;
+        }
+        out[i] = from_f32<T>(v);
+    }
+}
+
+__global__ void flush_kernel(uint4 *__restrict__ p, uint64_t n16, uint32_t salt) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride)
+        p[i] = make_uint4((uint32_t)i, salt, (uint32_t)(i >> 32), ~salt);
+}
+
+}  // namespace
+
+LaunchFn make_row_kernel(Context *ctx, const Spec &s, std::string &impl) {
+    const uint64_t n = s.len;
+    switch (s.op) {
+        case Op::Axpy: {
+            const int grid = grid_for(ctx, (n + 3) / 4, kThreads);
+            const float alpha = s.alpha;
+            impl = "axpy_f32_v4";
+            return [=](cudaStream_t st, void **b) {
+                axpy_kernel<<<grid, kThreads, 0, st>>>((const float *)b[0], (const float *)b[1], (float *)b[2], alpha, n);
+                return cudaGetLastError();
+            };
+        }
+        case Op::Add: {
+            const int grid = grid_for(ctx, (n + 3) / 4, kThreads);
+            impl = "add_f32_v4";
+            return [=](cudaStream_t st, void **b) {
+                add_kernel<<<grid, kThreads, 0, st>>>((const float *)b[0], (const float *)b[1], (float *)b[2], n);
+                return cudaGetLastError();
+            };
+        }
+        case Op::SwiGlu: {
+            if (s.dtype == DType::BF16) {
+                const int grid = grid_for(ctx, (n + 7) / 8, kThreads);
+                impl = "swiglu_bf16_v8";
+                return [=](cudaStream_t st, void **b) {
+                    swiglu_bf16_kernel<<<grid, kThreads, 0, st>>>((const __nv_bfloat16 *)b[0], (const __nv_bfloat16 *)b[1], (__nv_bfloat16 *)b[2], n);
+                    return cudaGetLastError();
+                };
+            }
+            const int grid = grid_for(ctx, (n + 3) / 4, kThreads);
+            impl = "swiglu_f32_v4";
+            return [=](cudaStream_t st, void **b) {
+                swiglu_f32_kernel<<<grid, kThreads, 0, st>>>((const float *)b[0], (const float *)b[1], (float *)b[2], n);
+                return cudaGetLastError();
+            };
+        }
+        case Op::RmsNorm:
+            return s.dtype == DType::BF16 ? row_launch<__nv_bfloat16, RowOp::RmsNorm>(ctx, s, impl) : row_launch<float, RowOp::RmsNorm>(ctx, s, impl);
+        case Op::Softmax:
+            return s.dtype == DType::BF16 ? row_launch<__nv_bfloat16, RowOp::Softmax>(ctx, s, impl) : row_launch<float, RowOp::Softmax>(ctx, s, impl);
+        case Op::RmsInv:
+            return s.dtype == DType::BF16 ? row_launch<__nv_bfloat16, RowOp::RmsInv>(ctx, s, impl) : row_launch<float, RowOp::RmsInv>(ctx, s, impl);
+        default: throw IrError("not a row kernel");
+    }
+}
+
+LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl) {
+    if (s.op == Op::Fill) {
+        const uint64_t n = s.len, seed = s.seed;
+        const uint32_t stream = s.stream_id;
+        const int normal = s.dist == "normal";
+        const float lo = s.lo, hi = s.hi;
+        const int grid = grid_for(ctx, n, kThreads);
+        impl = std::string("fill_") + s.dist + "_" + dtype_name(s.dtype);
+        const DType d = s.dtype;
+        return [=](cudaStream_t st, void **b) {
+            if (d == DType::BF16) fill_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>((__nv_bfloat16 *)b[0], n, seed, stream, normal, lo, hi);
+            else if (d == DType::F16) fill_kernel<__half><<<grid, kThreads, 0, st>>>((__half *)b[0], n, seed, stream, normal, lo, hi);
+            else fill_kernel<float><<<grid, kThreads, 0, st>>>((float *)b[0], n, seed, stream, normal, lo, hi);
+            return cudaGetLastError();
+        };
+    }
+    if (s.op == Op::L2Flush) {
+        const uint64_t n16 = s.bytes / 16;
+        const int grid = grid_for(ctx, n16, kThreads, 4);
+        impl = "l2_flush";
+        auto salt = std::make_shared<uint32_t>(1);
+        return [=](cudaStream_t st, void **b) {
+            flush_kernel<<<grid, kThreads, 0, st>>>((uint4 *)b[0], n16, (*salt)++);
+            return cudaGetLastError();
+        };
+    }
+    throw IrError("not a utility kernel");
+}
+
+}  // namespace jade
