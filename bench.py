@@ -1,0 +1,317 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path: causal attention TFLOP/s on BASELINE config 2
+(B=4, H=16, S=2048, D=128, BF16 N(0,1), O in BF16), through the C ABI.
+
+Contract (one JSON line on rank 0):
+  value      device-timed throughput of the attention kernel, inputs resident in
+             HBM, L2 flushed (256 MiB write) between steps; max over ranks.
+  e2e        the same metric through the public API with host buffers: each step
+             copies Q, K, V from pinned host memory, runs attention and copies O
+             back, all as jobs of one ordered batch, event-timed on the stream.
+  roofline   tensor-bound: algorithmic FLOPs per launch / mean launch time vs the
+             measured dense BF16 peak; traffic from the committed ncu summary.
+  cpu_baseline  the FP64 oracle (the reference's CPU attention restated,
+             metal_lab.rs:33-73) on a bounded sample of rows, all host threads.
+  components GEMM 8192^3 BF16 (BASELINE targets), non-causal attention.
+Multi-GPU: one process per GPU (torchrun); each rank runs its own batch x head
+shard (weak scaling, no collective on the data path).
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle port) on the host cores instead and prints the same metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GEMM & causal-attention TFLOP/s, MLP-block tokens/s at 1/2/4/8 B200"
+B, H, S, D = 4, 16, 2048, 128
+
+
+def causal_flops(b, h, s, d):
+    # exact kept (query, key) pairs: s(s+1)/2 per head; QK^T and PV are 2*d each
+    return 2.0 * b * h * s * (s + 1) * d
+
+
+def full_flops(b, h, s, d):
+    return 4.0 * b * h * s * s * d
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p.get("hbm_gbs", 6650.0), "bf16": p.get("bf16_tflops", 1590.0),
+                "bf16_sustained": p.get("bf16_tflops_sustained", 1400.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic(kernel_key):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(kernel_key)
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, device):
+        self.samples, self.reasons, self.stop = [], set(), threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.nv:
+            self.stop.set()
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        return dist, world, rank, local
+    return None, 1, 0, 0
+
+
+def reduce_max(dist, x):
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- CPU
+def cpu_attention_sample(seconds, threads, seed=0):
+    """Times the FP64 oracle attention (causal, C2 shape) on a sample of rows sized
+    to about `seconds`; returns (TFLOP/s, description, threads)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    n = S * D
+    q = rng.standard_normal(n).astype(np.float32)
+    k = rng.standard_normal(n).astype(np.float32)
+    v = rng.standard_normal(n).astype(np.float32)
+    q, k, v = (O.round_bf16(x) for x in (q, k, v))
+
+    def run(rows):
+        bh = np.zeros(len(rows), np.int64)
+        t0 = time.perf_counter()
+        O.attention_rows(S, D, True, q, k, v, bh, rows, threads=threads)
+        dt = time.perf_counter() - t0
+        return sum(4.0 * D * (int(r) + 1) for r in rows) / dt, dt
+
+    probe = rng.integers(0, S, 8 * threads)
+    rate, dt = run(probe)
+    per_row = dt / len(probe)
+    count = max(threads, int(seconds / max(per_row, 1e-9)))
+    rows = rng.integers(0, S, count)
+    rate, dt = run(rows)
+    return rate / 1e12, f"{count} random causal rows of one head (S={S}, D={D}), FP64 materialized, {dt:.1f} s", threads
+
+
+def run_reference(args):
+    dist, world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    threads = O.max_threads()
+    per_step = max(1.0, min(10.0, 60.0 / max(args.steps + args.warmup, 1)))
+    for _ in range(args.warmup):
+        cpu_attention_sample(per_step / 4, threads, seed=1)
+    rates, descs, t0 = [], [], time.perf_counter()
+    for i in range(args.steps):
+        r, desc, _ = cpu_attention_sample(per_step, threads, seed=2 + i)
+        rates.append(r)
+        descs.append(desc)
+    wall = time.perf_counter() - t0
+    value = statistics.median(rates)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"causal attention B={B} H={H} S={S} D={D} (BASELINE configs[1]), CPU oracle port",
+                       "global_batch": B, "seq_len": S, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": descs[0]},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU
+def attention_bench(rt, jc, steps, warmup, causal, batch):
+    n = batch * H * S * D
+    q, k, v, o = (rt.alloc(n, "bf16") for _ in range(4))
+    for i, buf in enumerate((q, k, v)):
+        rt.fill(buf, "normal", seed=1234, stream=i + 10 * (rt.device + 1), lo=0.0, hi=1.0)
+    flush_buf = rt.alloc_bytes(256 << 20)
+    flush = rt.compile({"op": "l2_flush", "bytes": 256 << 20})
+    attn = rt.compile({"op": "attention_online", "heads": H, "seq": S, "dim": D, "causal": causal, "dtype": "bf16",
+                       "batch": batch})
+    jobs = [(flush, [flush_buf]), (attn, [q, k, v, o])]
+    rt.execute(jobs, repeats=max(warmup, 3))
+    return jobs, attn, (q, k, v, o), flush_buf
+
+
+def gemm_bench(rt, steps, warmup, m=8192):
+    a, b, c = rt.alloc(m * m, "bf16"), rt.alloc(m * m, "bf16"), rt.alloc(m * m, "bf16")
+    rt.fill(a, "uniform", seed=5, stream=0, lo=-1, hi=1)
+    rt.fill(b, "uniform", seed=5, stream=1, lo=-1, hi=1)
+    g = rt.compile({"op": "gemm", "m": m, "n": m, "k": m, "tiled": True, "dtype": "bf16", "out_dtype": "bf16"})
+    rt.execute([(g, [a, b, c])], repeats=max(warmup, 3))
+    t = rt.execute([(g, [a, b, c])], repeats=steps, per_job=True)
+    ms = t.job_ms[0] / steps
+    tflops = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
+    for x in (a, b, c):
+        x.free()
+    return {"workload": f"GEMM {m}^3 BF16 in, FP32 accumulate, BF16 out (BASELINE configs[4])", "value": tflops,
+            "unit": "TFLOP/s", "ms_per_step": ms, "impl": g.info.get("impl")}
+
+
+def run_ours(args):
+    dist, world, rank, local = dist_setup()
+    import jade_compute_b200 as jc
+    peaks = load_peaks()
+    rt = jc.Runtime(local)
+    try:
+        jobs, attn, (q, k, v, o), flush_buf = attention_bench(rt, jc, args.steps, args.warmup, True, B)
+        flops = causal_flops(B, H, S, D)
+        barrier(dist)
+        with ClockSampler(local) as clk:
+            t = rt.execute(jobs, repeats=args.steps, per_job=True)
+        attn_ms_total = t.job_ms[1]
+        region_ms = t.gpu_ms
+        attn_ms_total = reduce_max(dist, attn_ms_total)
+        ms_step = attn_ms_total / args.steps
+        value = world * flops / (ms_step * 1e-3) / 1e12
+        per_gpu = flops / (ms_step * 1e-3) / 1e12
+        # end to end through the public API with host buffers
+        n = B * H * S * D
+        hq, hk, hv, ho = (rt.host_alloc(n, "bf16") for _ in range(4))
+        for hb, db in ((hq, q), (hk, k), (hv, v)):
+            hb.host_view()[:] = rt.download(db)
+        h2d = rt.compile({"op": "copy", "bytes": 2 * n, "direction": "h2d"})
+        d2h = rt.compile({"op": "copy", "bytes": 2 * n, "direction": "d2h"})
+        e2e_jobs = [(h2d, [hq, q]), (h2d, [hk, k]), (h2d, [hv, v]), (attn, [q, k, v, o]), (d2h, [o, ho])]
+        rt.execute(e2e_jobs, repeats=2)
+        e2e_steps = max(3, min(args.steps, 50))
+        barrier(dist)
+        te = rt.execute(e2e_jobs, repeats=e2e_steps, per_job=True)
+        e2e_ms = reduce_max(dist, te.gpu_ms) / e2e_steps
+        e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
+        components = []
+        if not args.quick:
+            components.append(gemm_bench(rt, max(5, min(args.steps, 20)), args.warmup))
+            jobs_f, attn_f, bufs_f, fb = attention_bench(rt, jc, args.steps, args.warmup, False, B)
+            tf = rt.execute(jobs_f, repeats=max(5, min(args.steps, 50)), per_job=True)
+            ms_f = tf.job_ms[1] / max(5, min(args.steps, 50))
+            components.append({"workload": f"non-causal attention B={B} H={H} S={S} D={D} BF16", "unit": "TFLOP/s",
+                               "value": full_flops(B, H, S, D) / (ms_f * 1e-3) / 1e12, "ms_per_step": ms_f})
+        cpu = None
+        if rank == 0 and not args.no_cpu:
+            from oracle import oracle as O
+            thr = O.max_threads()
+            rate, desc, cores = cpu_attention_sample(args.cpu_seconds, thr)
+            cpu = {"value": rate, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": desc}
+        achieved = per_gpu
+        traffic = load_traffic("attention_causal_c2")
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (counter-based N(0,1), BF16)",
+            "config": {"workload": f"causal attention B={B} H={H} S={S} D={D} BF16, O BF16 (BASELINE configs[1])",
+                       "global_batch": B * world, "seq_len": S, "heads": H, "head_dim": D,
+                       "parallelism": f"batch x head shards over {world} GPU(s), no collective",
+                       "l2": "flushed between steps (256 MiB write)", "flops_per_step_per_gpu": flops,
+                       "kernel": attn.info.get("impl")},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16"], "peak_source": peaks["source"] + " burst bf16",
+                         "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * 2 * n, "d2h_bytes_per_step": 2 * n,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+            "region_ms": region_ms,
+            "components": components,
+        }
+        if rank == 0:
+            print(json.dumps(line))
+    finally:
+        rt.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--quick", action="store_true", help="headline only, no components")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,439 @@
+// tcgen05 GEMM for BF16 / FP16 / TF32 inputs with FP32 accumulation in tensor
+// memory (TMEM), fed by TMA, persistent and warp-specialised.
+//
+// Reference semantics: C = A.B row-major, A [M,K], B [K,N] (src/runtime/ir.rs:298-303,
+// 524-557); the reference computes it with SIMT FP32 FMAs only. Extensions for
+// the residual MLP (src/runtime/workloads.rs:422-465): B may be stored [N,K]
+// (pre-transposed weights), each output row may be scaled by a per-row FP32
+// factor (RMSNorm folded in as diag(inv_rms) . x . (diag(w) W)), and the epilogue
+// may apply SwiGLU to a gate/up column pair or add a residual.
+//
+// Design:
+//   * CTA tile 128 x 256 (one tcgen05.mma.cta_group::1 M=128,N=256), K step of
+//     128 bytes per row (64 BF16/FP16 or 32 TF32 elements), 4-stage TMA ring of
+//     48 KB stages in 128-byte-swizzled shared memory, one CTA per SM.
+//   * warp 0: TMA producer; warp 1: MMA issuer (one elected lane); warps 2-5:
+//     epilogue (each owns one 32-lane quarter of TMEM = 32 output rows).
+//   * two 256-column FP32 accumulators in TMEM (all 512 columns), so the epilogue
+//     of tile i overlaps the MMAs of tile i+1.
+//   * grouped tile raster (8 M-blocks per group) for L2 reuse of A and B.
+//   * every mbarrier wait is bounded (common.cuh); the MMA lane drains its own
+//     tcgen05 work and the producer its TMA copies before TMEM is freed.
+#include <cuda.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "internal.hpp"
+
+namespace jade {
+namespace {
+
+constexpr int BM = 128, BN = 256, kStages = 4, kThreads = 192;
+constexpr uint32_t kStageA = BM * 128, kStageB = BN * 128, kStageBytes = kStageA + kStageB;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+enum Epi { kEpiNone = 0, kEpiSwiglu = 1, kEpiResidual = 2 };
+
+struct GemmArgs {
+    void *out;
+    const float *row_scale;
+    const void *residual;
+    int M, N, K;  // N = output columns
+    int tiles_m, tiles_n, num_tiles, kblocks;
+    int *err;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
+    constexpr int kGroup = 8;
+    const int per_group = kGroup * tiles_n;
+    const int g = t / per_group, first_m = g * kGroup;
+    const int gm = min(tiles_m - first_m, kGroup);
+    const int r = t % per_group;
+    tm = first_m + r % gm;
+    tn = r / gm;
+}
+
+template <typename TOut>
+__device__ __forceinline__ void store32(TOut *dst, const float (&v)[32], int valid, bool vec_ok);
+template <>
+__device__ __forceinline__ void store32<float>(float *dst, const float (&v)[32], int valid, bool vec_ok) {
+    if (valid >= 32 && vec_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < valid) dst[j] = v[j];
+    }
+}
+template <typename T16>
+__device__ __forceinline__ void store32_16(T16 *dst, const float (&v)[32], int valid, bool vec_ok) {
+    if (valid >= 32 && vec_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            uint4 u;
+            if constexpr (std::is_same<T16, __nv_bfloat16>::value) {
+                u.x = pack_bf16(v[j], v[j + 1]); u.y = pack_bf16(v[j + 2], v[j + 3]);
+                u.z = pack_bf16(v[j + 4], v[j + 5]); u.w = pack_bf16(v[j + 6], v[j + 7]);
+            } else {
+                u.x = pack_f16(v[j], v[j + 1]); u.y = pack_f16(v[j + 2], v[j + 3]);
+                u.z = pack_f16(v[j + 4], v[j + 5]); u.w = pack_f16(v[j + 6], v[j + 7]);
+            }
+            *reinterpret_cast<uint4 *>(dst + j) = u;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < valid) dst[j] = from_f32<T16>(v[j]);
+    }
+}
+template <>
+__device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16 *dst, const float (&v)[32], int valid, bool vec_ok) {
+    store32_16(dst, v, valid, vec_ok);
+}
+template <>
+__device__ __forceinline__ void store32<__half>(__half *dst, const float (&v)[32], int valid, bool vec_ok) {
+    store32_16(dst, v, valid, vec_ok);
+}
+
+template <int kEB, uint32_t kFmt, bool kBmn, typename TOut, int kEpi, bool kRowScale>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+    constexpr int BK = 128 / kEB;          // elements per 128-byte row
+    constexpr int UK = 32 / kEB;           // K per tcgen05.mma (32 bytes)
+    constexpr int kSteps = BK / UK;        // 4
+    constexpr uint32_t kIdesc = idesc_f32acc(kFmt, kFmt, false, kBmn, BM, BN);
+    constexpr int kBoxMN = 128 / kEB;      // MN-major B: elements per box row
+    constexpr int kBoxesB = BN / kBoxMN;   // MN-major B: boxes per stage
+    constexpr uint32_t kBoxBytesB = kBoxMN * kEB * BK;  // MN-major B: bytes per box (= BK rows x 128 B)
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *acc_full = empty + kStages;
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&acc_full[a], 1); mbar_init(&acc_empty[a], 128); }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        fence_proxy_async();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    int *err = args.err;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool issued[kStages] = {};
+            uint32_t last_phase[kStages] = {};
+            for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+                int tm, tn;
+                tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+                const int m0 = tm * BM, nb0 = tn * BN;  // B rows (nk) or columns (kn) of this tile
+                for (int kb = 0; kb < args.kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
+                    uint8_t *sa = smem + stage * kStageBytes;
+                    uint8_t *sb = sa + kStageA;
+                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+                    if constexpr (kBmn) {
+#pragma unroll
+                        for (int j = 0; j < kBoxesB; ++j) tma_load_2d(sb + j * kBoxBytesB, &tmB, &full[stage], nb0 + j * kBoxMN, kb * BK);
+                    } else {
+                        tma_load_2d(sb, &tmB, &full[stage], kb * BK, nb0);
+                    }
+                    issued[stage] = true;
+                    last_phase[stage] = phase;
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (*abort_flag)
+                for (int s = 0; s < kStages; ++s)
+                    if (issued[s]) mbar_wait_drain(&full[s], last_phase[s], err);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrWaitAccEmpty)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                bool ok = true;
+                for (int kb = 0; kb < args.kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrWaitTmaFull)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+                    const uint32_t sb = sa + kStageA;
+#pragma unroll
+                    for (int k = 0; k < kSteps; ++k) {
+                        const uint64_t adesc = sdesc_sw128(sa + k * 32, 16, 1024);
+                        uint64_t bdesc;
+                        if constexpr (kBmn) bdesc = sdesc_sw128(sb + k * UK * 128, kBoxBytesB, 1024);
+                        else bdesc = sdesc_sw128(sb + k * 32, 16, 1024);
+                        umma<kFmt == 2>(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+                    }
+                    umma_commit(&empty[stage]);  // frees the stage when these MMAs finish reading it
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+            }
+            umma_commit(mma_done);  // all tcgen05 work of this thread, done or aborted
+            mbar_wait_drain(mma_done, 0, err);
+        }
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..5)
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const int row_in_tile = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+            int tm, tn;
+            tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+            if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrWaitAccFull)) break;
+            tc_fence_after();
+            const int row = tm * BM + row_in_tile;
+            const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+            const float scale = (kRowScale && row < args.M) ? args.row_scale[row] : 1.0f;
+            TOut *out = static_cast<TOut *>(args.out);
+            if constexpr (kEpi == kEpiSwiglu) {
+                const int c0 = tn * 128;
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 32) {
+                    uint32_t g[32], u[32];
+                    tmem_ld32(tbase + c, g);
+                    tmem_ld32(tbase + 128 + c, u);
+                    tmem_wait_ld();
+                    float h[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float gv = __uint_as_float(g[j]) * scale, uv = __uint_as_float(u[j]) * scale;
+                        h[j] = (gv * stable_sigmoid(gv)) * uv;
+                    }
+                    const int col = c0 + c;
+                    if (row < args.M && col < args.N)
+                        store32<TOut>(out + (size_t)row * args.N + col, h, args.N - col, (args.N % 8) == 0);
+                }
+            } else {
+                const int c0 = tn * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    const int col = c0 + c;
+                    if (col >= args.N) break;  // uniform across the warp
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c, r);
+                    tmem_wait_ld();
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+                    if (row < args.M) {
+                        if constexpr (kEpi == kEpiResidual) {
+                            const TOut *res = static_cast<const TOut *>(args.residual) + (size_t)row * args.N + col;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col + j < args.N) v[j] += to_f32(res[j]);
+                        }
+                        store32<TOut>(out + (size_t)row * args.N + col, v, args.N - col, (args.N % 8) == 0);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *, const cuuint64_t *,
+                              const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encoder() {
+    static EncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] { fn = reinterpret_cast<EncodeFn>(driver_entry("cuTensorMapEncodeTiled")); });
+    return fn;
+}
+
+// 2-D row-major tensor [rows, cols], box {box_cols, box_rows}, 128-byte swizzle.
+bool make_map(CUtensorMap *map, CUtensorMapDataType dt, int eb, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_cols,
+              uint32_t box_rows) {
+    EncodeFn enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * (uint64_t)eb};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int kEB, uint32_t kFmt, bool kBmn, typename TOut, int kEpi, bool kRowScale>
+LaunchFn tc_launch(Context *ctx, const Spec &s) {
+    auto kernel = gemm_tc_kernel<kEB, kFmt, kBmn, TOut, kEpi, kRowScale>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+        throw IrError("cannot reserve shared memory for the tcgen05 GEMM");
+    const CUtensorMapDataType dt = kFmt == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : kFmt == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    GemmArgs base{};
+    base.M = (int)s.m;
+    base.N = (int)s.n;
+    base.K = (int)s.k;
+    const bool swiglu = kEpi == kEpiSwiglu;
+    const uint64_t brows = swiglu ? 2ull * s.n : s.n;  // rows of B in nk layout / cols in kn layout
+    base.tiles_m = (int)((s.m + BM - 1) / BM);
+    base.tiles_n = swiglu ? (int)(s.n / 128) : (int)((s.n + BN - 1) / BN);
+    base.num_tiles = base.tiles_m * base.tiles_n;
+    base.kblocks = (int)((s.k + (128 / kEB) - 1) / (128 / kEB));
+    base.err = ctx->err_dev;
+    const int grid = std::min(base.num_tiles, ctx->sm_count);
+    const uint64_t M = s.m, K = s.k;
+    return [=](cudaStream_t st, void **b) {
+        CUtensorMap ma, mb;
+        if (!make_map(&ma, dt, kEB, b[0], M, K, 128 / kEB, BM)) return cudaErrorInvalidValue;
+        const bool okb = kBmn ? make_map(&mb, dt, kEB, b[1], K, brows, 128 / kEB, 128 / kEB)
+                              : make_map(&mb, dt, kEB, b[1], brows, K, 128 / kEB, BN);
+        if (!okb) return cudaErrorInvalidValue;
+        GemmArgs a = base;
+        int idx = 2;
+        a.row_scale = kRowScale ? static_cast<const float *>(b[idx++]) : nullptr;
+        a.residual = kEpi == kEpiResidual ? b[idx++] : nullptr;
+        a.out = b[idx];
+        kernel<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, a);
+        return cudaGetLastError();
+    };
+}
+
+template <int kEB, uint32_t kFmt, typename TOut, typename T16>
+LaunchFn pick_epilogue(Context *ctx, const Spec &s) {
+    if (s.epilogue == "swiglu") {
+        if (s.row_scale) return tc_launch<kEB, kFmt, false, TOut, kEpiSwiglu, true>(ctx, s);
+        return tc_launch<kEB, kFmt, false, TOut, kEpiSwiglu, false>(ctx, s);
+    }
+    if (s.epilogue == "residual") {
+        if (s.b_nk) {
+            if (s.row_scale) return tc_launch<kEB, kFmt, false, TOut, kEpiResidual, true>(ctx, s);
+            return tc_launch<kEB, kFmt, false, TOut, kEpiResidual, false>(ctx, s);
+        }
+        return tc_launch<kEB, kFmt, true, TOut, kEpiResidual, false>(ctx, s);
+    }
+    if (s.b_nk) {
+        if (s.row_scale) return tc_launch<kEB, kFmt, false, TOut, kEpiNone, true>(ctx, s);
+        return tc_launch<kEB, kFmt, false, TOut, kEpiNone, false>(ctx, s);
+    }
+    if (s.row_scale) return tc_launch<kEB, kFmt, true, TOut, kEpiNone, true>(ctx, s);
+    return tc_launch<kEB, kFmt, true, TOut, kEpiNone, false>(ctx, s);
+}
+
+// FP32 [rows, cols] -> [cols, rows] through 32x32 shared-memory tiles.
+__global__ void transpose_f32(const float *__restrict__ in, float *__restrict__ out, int rows, int cols) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = in[(size_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) out[(size_t)c * rows + r] = tile[threadIdx.x][i];
+    }
+}
+
+// Device workspace owned by a compiled kernel, released with it.
+struct Workspace {
+    void *ptr = nullptr;
+    int device = 0;
+    ~Workspace() {
+        if (ptr) {
+            cudaSetDevice(device);
+            cudaFree(ptr);
+        }
+    }
+};
+
+}  // namespace
+
+bool gemm_tc_supports(const Spec &s, std::string &why) {
+    const uint64_t eb = dtype_size(s.dtype);
+    if (s.op != Op::Gemm || s.dtype == DType::F32) { why = "not a tensor-core dtype"; return false; }
+    if ((s.k * eb) % 16) { why = "TMA needs K * element size to be a multiple of 16 bytes"; return false; }
+    if (!s.b_nk && (s.n * eb) % 16) { why = "TMA needs N * element size to be a multiple of 16 bytes for B [K,N]"; return false; }
+    if (!encoder()) { why = "cuTensorMapEncodeTiled unavailable"; return false; }
+    return true;
+}
+
+LaunchFn make_gemm_tc(Context *ctx, const Spec &s, std::string &impl) {
+    std::string why;
+    if (!gemm_tc_supports(s, why)) throw IrError(why);
+    impl = std::string("gemm_tcgen05_128x256_") + dtype_name(s.dtype) + (s.b_nk ? "_nk" : "_kn") + "_out_" + dtype_name(s.out_dtype) +
+           (s.epilogue != "none" ? "_" + s.epilogue : std::string()) + (s.row_scale ? "_rowscale" : "");
+    switch (s.dtype) {
+        case DType::TF32:
+            if (!s.b_nk) {
+                // MN-major TF32 operands need the 32-byte-atom swizzle; B [K,N] is
+                // instead transposed once per launch into a [N,K] workspace (K-major),
+                // a 2*K*N*4-byte pass that is part of every launch.
+                Spec t = s;
+                t.b_nk = true;
+                LaunchFn inner = pick_epilogue<4, 2, float, float>(ctx, t);
+                auto ws = std::make_shared<Workspace>();
+                ws->device = ctx->device;
+                if (cudaMalloc(&ws->ptr, (size_t)s.k * s.n * 4) != cudaSuccess) {
+                    cudaGetLastError();
+                    throw IrError("cannot allocate the TF32 B-transpose workspace");
+                }
+                impl += "_transposeB";
+                const int K = (int)s.k, N = (int)s.n;
+                const bool extra = s.row_scale || s.epilogue == "residual";
+                return [=](cudaStream_t st, void **b) {
+                    transpose_f32<<<dim3((N + 31) / 32, (K + 31) / 32), dim3(32, 8), 0, st>>>((const float *)b[0 + 1], (float *)ws->ptr, K, N);
+                    void *nb[5] = {b[0], ws->ptr, b[2], extra ? b[3] : nullptr, extra ? b[4] : nullptr};
+                    return inner(st, nb);
+                };
+            }
+            return pick_epilogue<4, 2, float, float>(ctx, s);
+        case DType::BF16:
+            if (s.out_dtype == DType::BF16) return pick_epilogue<2, 1, __nv_bfloat16, __nv_bfloat16>(ctx, s);
+            return pick_epilogue<2, 1, float, __nv_bfloat16>(ctx, s);
+        case DType::F16:
+            if (s.out_dtype == DType::F16) return pick_epilogue<2, 0, __half, __half>(ctx, s);
+            return pick_epilogue<2, 0, float, __half>(ctx, s);
+        default: throw IrError("unsupported tensor-core dtype");
+    }
+}
+
+}  // namespace jade

@@ -1,0 +1,134 @@
+"""GPU parity of the tcgen05 GEMM (BF16 / FP16 / TF32 inputs, FP32 accumulate).
+
+Oracle: src/validation.rs:35-91 (FP64 dot products over the same rounded inputs,
+tolerance 2e-5 + coef * sum|a*b|) restated in oracle/oracle.c. For 16-bit inputs
+the oracle consumes the stored 16-bit values widened to FP64, so the only error
+left is FP32 accumulation (coef = max(2*K*eps32, 2e-6)); TF32 inputs are read
+from FP32 storage and truncated inside the tensor core, covered by the
+reference's reduced-precision coefficient 0.0012. 16-bit outputs add their own
+rounding (2^-8 relative), checked with workloads.rs:224-243 ``compare``.
+"""
+import numpy as np
+import pytest
+
+import jade_compute_b200 as jc
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt():
+    r = jc.Runtime(0)
+    yield r
+    r.close()
+
+
+def operands(rt, m, n, k, dtype, b_nk, seed, nb=None):
+    nb = n if nb is None else nb
+    a = rt.alloc(m * k, dtype)
+    b = rt.alloc(k * nb, dtype)
+    rt.fill(a, "uniform", seed=seed, stream=0, lo=-1.0, hi=1.0)
+    rt.fill(b, "uniform", seed=seed, stream=1, lo=-1.0, hi=1.0)
+    af, bf = rt.download_f32(a), rt.download_f32(b)
+    if b_nk:  # stored [N,K]; the oracle wants [K,N]
+        bf_kn = np.ascontiguousarray(bf.reshape(nb, k).T).ravel()
+    else:
+        bf_kn = bf
+    return a, b, af, bf_kn
+
+
+SHAPES = [(128, 256, 64), (128, 256, 128), (256, 512, 512), (1, 8, 8), (33, 40, 24), (200, 300, 136),
+          (129, 257, 1024), (512, 768, 4096), (1024, 1024, 1024)]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16", "tf32"])
+@pytest.mark.parametrize("b_nk", [False, True], ids=["kn", "nk"])
+@pytest.mark.parametrize("mnk", SHAPES, ids=str)
+def test_tc_gemm_fp32_out(rt, dtype, b_nk, mnk):
+    m, n, k = mnk
+    a, b, af, bf = operands(rt, m, n, k, dtype, b_nk, seed=m * 7 + n * 3 + k)
+    out = rt.alloc(m * n)
+    spec = {"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": dtype, "b_layout": "nk" if b_nk else "kn"}
+    kern = rt.compile(spec)
+    if (k * (4 if dtype == "tf32" else 2)) % 16 == 0 and (b_nk or (n * (4 if dtype == "tf32" else 2)) % 16 == 0):
+        assert kern.info["path"] == "tcgen05", kern.info
+    rt.execute([(kern, [a, b, out])], repeats=2)
+    got = rt.download(out)
+    rc, v = O.validation_check(m, n, k, af, bf, got, budget=1 << 14, fp16=(dtype == "tf32"))
+    assert rc == 0, (rc, v.first_bad_index, v.max_scaled_error, kern.info["impl"])
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_tc_gemm_16bit_out(rt, dtype):
+    m, n, k = 384, 512, 640
+    a, b, af, bf = operands(rt, m, n, k, dtype, False, seed=3)
+    out = rt.alloc(m * n, dtype)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": dtype, "out_dtype": dtype})
+    rt.execute([(kern, [a, b, out])])
+    exp = O.gemm_reference(m, n, k, af, bf)
+    scale = np.abs(exp).max()
+    rc, r = O.compare(rt.download_f32(out), exp, 2e-3 * scale, 2 ** -8)
+    assert rc == 0, r.max_abs_error
+
+
+def test_tc_gemm_row_scale_and_residual(rt):
+    m, n, k = 256, 512, 384
+    a, b, af, bf = operands(rt, m, n, k, "bf16", True, seed=9)
+    scale = rt.alloc(m)
+    rt.fill(scale, "uniform", seed=9, stream=4, lo=0.5, hi=2.0)
+    res = rt.alloc(m * n)
+    rt.fill(res, "normal", seed=9, stream=5, lo=0.0, hi=1.0)
+    out = rt.alloc(m * n)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": "bf16", "b_layout": "nk",
+                       "row_scale": True, "epilogue": "residual"})
+    rt.execute([(kern, [a, b, scale, res, out])])
+    exp = O.gemm_reference(m, n, k, af, bf).reshape(m, n) * rt.download(scale).astype(np.float64)[:, None] \
+        + rt.download(res).astype(np.float64).reshape(m, n)
+    rc, r = O.compare(rt.download(out), exp.ravel(), 1e-4, 1e-4)
+    assert rc == 0, r.max_abs_error
+
+
+@pytest.mark.parametrize("out_dtype", ["fp32", "bf16"])
+def test_tc_gemm_swiglu_epilogue(rt, out_dtype):
+    # gate/up weights interleaved in blocks of 128 rows: [g0..g127, u0..u127, g128.., ...]
+    m, n, k = 200, 384, 256
+    a, b, af, bf_kn = operands(rt, m, n, k, "bf16", True, seed=21, nb=2 * n)
+    inv = rt.alloc(m)
+    rt.fill(inv, "uniform", seed=21, stream=3, lo=0.5, hi=1.5)
+    out = rt.alloc(m * n, out_dtype)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": "bf16", "b_layout": "nk",
+                       "epilogue": "swiglu", "row_scale": True, "out_dtype": out_dtype})
+    assert kern.info["path"] == "tcgen05"
+    rt.execute([(kern, [a, b, inv, out])])
+    W = bf_kn.reshape(k, 2 * n)  # [K, 2N] with interleaved column blocks
+    cols = np.arange(2 * n).reshape(-1, 2, 128)
+    gate_cols, up_cols = cols[:, 0, :].ravel(), cols[:, 1, :].ravel()
+    A = af.reshape(m, k).astype(np.float64) * rt.download(inv).astype(np.float64)[:, None]
+    g = A @ W[:, gate_cols].astype(np.float64)
+    u = A @ W[:, up_cols].astype(np.float64)
+    h = g / (1 + np.exp(-g)) * u
+    tol = (1e-4, 1e-4) if out_dtype == "fp32" else (2e-3 * np.abs(h).max(), 2 ** -8)
+    rc, r = O.compare(rt.download_f32(out), h.ravel(), *tol)
+    assert rc == 0, r.max_abs_error
+
+
+def test_tc_gemm_is_deterministic_and_leaves_inputs(rt):
+    m, n, k = 512, 512, 512
+    a, b, af, bf = operands(rt, m, n, k, "bf16", False, seed=4)
+    out1, out2 = rt.alloc(m * n), rt.alloc(m * n)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": "bf16"})
+    rt.execute([(kern, [a, b, out1]), (kern, [a, b, out2])], repeats=3, graph=True)
+    assert np.array_equal(rt.download(out1), rt.download(out2))
+    assert np.array_equal(rt.download_f32(a), af)
+
+
+def test_unaligned_shapes_take_simt_path(rt):
+    m, n, k = 31, 47, 19  # K*2 bytes is not a multiple of 16: TMA cannot describe it
+    a, b, af, bf = operands(rt, m, n, k, "bf16", False, seed=5)
+    out = rt.alloc(m * n)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": "bf16"})
+    assert kern.info["path"] == "simt"
+    rt.execute([(kern, [a, b, out])])
+    rc, v = O.validation_check(m, n, k, af, bf, rt.download(out))
+    assert rc == 0
