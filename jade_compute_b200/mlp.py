@@ -1,0 +1,108 @@
+"""Residual MLP block on the B200 backend: the reference's six-op synthetic MLP
+(src/runtime/workloads.rs:366-525)
+
+    y = x + W_down . ( silu(W_gate . RMSNorm(x)) * (W_up . RMSNorm(x)) )
+
+as four ordered jobs instead of six dispatches:
+
+  1. rms_inv   inv[t] = 1/sqrt(mean(x_t^2) + eps)                (one read of x)
+  2. gemm      h = swiglu(diag(inv) . x . Wgu)   tcgen05, B = [gate|up] blocks of
+               128 rows interleaved, norm weight folded in (diag(w) W), SwiGLU and
+               the row scale applied in the epilogue; h written once in BF16
+  3. gemm      y = h . Wd (+ x on rank 0)      tcgen05, residual in the epilogue
+  4. all_reduce(y)                              NCCL, only when tensor-parallel
+
+Tensor parallelism over `tp` ranks splits ffn: rank r holds the gate/up columns
+and down-projection rows [r*ffn/tp, (r+1)*ffn/tp); the partial outputs are summed
+by one all-reduce after the down projection, the residual is added once (rank 0).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .runtime import Runtime, f32_to_bf16
+
+BLOCK = 128  # gate/up interleave granularity = half of the GEMM's 256-column tile
+
+
+def shard_columns(ffn: int, tp: int, rank: int) -> slice:
+    if ffn % tp or (ffn // tp) % BLOCK:
+        raise ValueError(f"ffn={ffn} must split into {tp} shards that are multiples of {BLOCK}")
+    w = ffn // tp
+    return slice(rank * w, (rank + 1) * w)
+
+
+def pack_gate_up(wg: np.ndarray, wu: np.ndarray, norm_weight: np.ndarray) -> np.ndarray:
+    """wg, wu: [d, f] (the reference's K x N layout) -> [2f, d] with rows
+    [gate block b | up block b] for b = 0..f/128-1, each row scaled by the norm weight."""
+    d, f = wg.shape
+    g = (wg * norm_weight[:, None]).T  # [f, d]
+    u = (wu * norm_weight[:, None]).T
+    out = np.empty((2 * f, d), dtype=np.float32)
+    for b in range(f // BLOCK):
+        out[2 * b * BLOCK:(2 * b + 1) * BLOCK] = g[b * BLOCK:(b + 1) * BLOCK]
+        out[(2 * b + 1) * BLOCK:(2 * b + 2) * BLOCK] = u[b * BLOCK:(b + 1) * BLOCK]
+    return out
+
+
+def unpack_gate_up(packed: np.ndarray, d: int):
+    """Inverse of pack_gate_up (norm weight left folded in): -> wg, wu as [d, f]."""
+    f = packed.shape[0] // 2
+    blocks = packed.reshape(f // BLOCK, 2, BLOCK, d)
+    return blocks[:, 0].reshape(f, d).T.copy(), blocks[:, 1].reshape(f, d).T.copy()
+
+
+class ResidualMLP:
+    """One tensor-parallel shard of the fused residual MLP, resident on one device."""
+
+    def __init__(self, rt: Runtime, tokens: int, width: int, hidden: int, tp: int = 1, rank: int = 0,
+                 eps: float = 1e-5, collective: bool = True):
+        self.rt, self.T, self.d, self.ffn, self.tp, self.rank, self.eps = rt, tokens, width, hidden, tp, rank, eps
+        self.f = hidden // tp
+        shard_columns(hidden, tp, rank)
+        T, d, f = tokens, width, self.f
+        self.x = rt.alloc(T * d, "bf16")
+        self.wgu = rt.alloc(2 * f * d, "bf16")
+        self.wd = rt.alloc(d * f, "bf16")
+        self.inv = rt.alloc(T, "fp32")
+        self.h = rt.alloc(T * f, "bf16")
+        self.y = rt.alloc(T * d, "bf16")
+        base = {"tiled": True, "dtype": "bf16", "b_layout": "nk", "out_dtype": "bf16"}
+        self.k_inv = rt.compile({"op": "rms_inv", "rows": T, "cols": d, "epsilon": eps, "dtype": "bf16"})
+        self.k_up = rt.compile({"op": "gemm", "m": T, "n": f, "k": d, "epilogue": "swiglu", "row_scale": True, **base})
+        down = {"op": "gemm", "m": T, "n": d, "k": f, **base}
+        if rank == 0:
+            down["epilogue"] = "residual"
+        self.k_down = rt.compile(down)
+        self.k_ar = rt.compile({"op": "all_reduce", "len": T * d, "dtype": "bf16"}) if tp > 1 and collective else None
+
+    def jobs(self):
+        j = [(self.k_inv, [self.x, self.inv]),
+             (self.k_up, [self.x, self.wgu, self.inv, self.h]),
+             (self.k_down, [self.h, self.wd, self.x, self.y] if self.rank == 0 else [self.h, self.wd, self.y])]
+        if self.k_ar is not None:
+            j.append((self.k_ar, [self.y]))
+        return j
+
+    def flops(self) -> float:
+        """Algorithmic FLOPs of this shard: 2*T*d*(2f) + 2*T*f*d."""
+        return 6.0 * self.T * self.d * self.f
+
+    # -- weights
+    def fill_synthetic(self, seed: int = 0, std: float = 0.02) -> None:
+        """BASELINE config 4 inputs: x ~ N(0,1), weights ~ N(0, std), norm weight 1
+        (so folding it is the identity); generated on device directly in the packed
+        layout, the shard's own stream of the counter-based generator."""
+        self.rt.fill(self.x, "normal", seed=seed, stream=0, lo=0.0, hi=1.0)
+        self.rt.fill(self.wgu, "normal", seed=seed, stream=100 + self.rank, lo=0.0, hi=std)
+        self.rt.fill(self.wd, "normal", seed=seed, stream=200 + self.rank, lo=0.0, hi=std)
+
+    def load(self, x, norm_weight, wg, wu, wd) -> None:
+        """Host FP32 weights in the reference's layout: wg, wu [d, ffn], wd [ffn, d]."""
+        cols = shard_columns(self.ffn, self.tp, self.rank)
+        self.rt.upload(self.x, f32_to_bf16(np.asarray(x, np.float32).ravel()))
+        wg = np.asarray(wg, np.float32).reshape(self.d, self.ffn)[:, cols]
+        wu = np.asarray(wu, np.float32).reshape(self.d, self.ffn)[:, cols]
+        self.rt.upload(self.wgu, f32_to_bf16(pack_gate_up(wg, wu, np.asarray(norm_weight, np.float32)).ravel()))
+        wd = np.asarray(wd, np.float32).reshape(self.ffn, self.d)[cols]
+        self.rt.upload(self.wd, f32_to_bf16(np.ascontiguousarray(wd.T).ravel()))  # [d, f] = nk layout
