@@ -134,6 +134,35 @@ JR_API int jr_comm_init(void *ctx, int nranks, int rank, const unsigned char id[
 JR_API int jr_comm_init_all(void **ctxs, int count, uint32_t timeout_ms, char *err, size_t cap);
 JR_API int jr_comm_destroy(void *ctx);
 
+/* Allocation-free TF32 GEMM: out[m,n] (FP32) = a[m,k] . b[k,n], a and b FP32
+ * row-major, computed on the tensor cores in TF32 with FP32 accumulation - the
+ * same kernels as a compiled {"op":"gemm","dtype":"tf32"} spec with the default
+ * b_layout "kn". No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory when they call: code running
+ * inside a host framework that owns every device allocation through its own
+ * pool, or a latency-critical loop where cudaMalloc's implicit device-wide
+ * synchronisation is not acceptable. The compiled path obtains its B-transpose
+ * workspace with cudaMalloc; this entry point instead uses a static 16 MiB
+ * device array built into the library, so it calls no cudaMalloc, cudaFree or
+ * other allocating routine, and needs no jr_create context.
+ *
+ *  - Limit: k * n <= 4,194,304 elements (16 MiB of FP32); larger shapes are
+ *    rejected with JR_EINVAL and a message. k must be a multiple of 4 and a, b
+ *    16-byte aligned. Every GPU that loads the library holds the 16 MiB until
+ *    the process exits.
+ *  - Runs on the current device. The first call on each device performs a
+ *    one-time set-up there (it looks up the array's device address); make that
+ *    first call before any stream capture.
+ *  - Enqueues on `stream` (NULL = the legacy default stream) and synchronises
+ *    it before returning; returns JR_ETIMEOUT if a device-side bounded wait
+ *    expired.
+ *  - Every call on a device shares the one array and it keeps the last call's
+ *    contents: calls whose GPU work overlaps (several host threads or streams at
+ *    once) race on it and must be serialised by the caller. */
+JR_API int jr_gemm_tf32_kn_noalloc(const float *a, const float *b, float *out, uint32_t m, uint32_t n, uint32_t k,
+                                   void *stream, char *err, size_t cap);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,9 +21,12 @@
 //     tcgen05 work and the producer its TMA copies before TMEM is freed.
 #include <cuda.h>
 
+#include <climits>
+#include <cstdio>
 #include <mutex>
 #include <type_traits>
 
+#include "../../include/jade_runtime.h"
 #include "common.cuh"
 #include "internal.hpp"
 
@@ -437,3 +440,108 @@ LaunchFn make_gemm_tc(Context *ctx, const Spec &s, std::string &impl) {
 }
 
 }  // namespace jade
+
+// ---------------------------------------------------------------------------
+// Allocation-free TF32 GEMM with B stored [K,N] (jr_gemm_tf32_kn_noalloc).
+//
+// The compiled path above transposes B into a workspace that jr_compile obtains
+// with cudaMalloc. Callers that must not allocate device memory at call time
+// (a plugin running inside a host framework that owns every device allocation
+// through its own pool, or a latency-critical loop where cudaMalloc's implicit
+// device synchronisation is unacceptable) use this entry point instead: its
+// scratch is a fixed, file-scope device array that every GPU loading this
+// library holds until process exit.
+namespace jade {
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;  // 16 MiB: K*N <= 4,194,304
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ int g_noalloc_error;  // bounded-wait expiry code of the last call
+
+struct NoAllocDevice {
+    bool ready = false;
+    float *scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    int *err = nullptr;        // device address of g_noalloc_error on this device
+    int sm_count = 0;
+};
+std::mutex g_noalloc_mutex;
+NoAllocDevice g_noalloc_devices[64];
+
+int noalloc_fail(int code, char *err, size_t cap, const char *msg) {
+    if (err && cap) {
+        snprintf(err, cap, "%s", msg);
+        err[cap - 1] = '\0';
+    }
+    return code;
+}
+
+}  // namespace
+}  // namespace jade
+
+extern "C" JR_API int jr_gemm_tf32_kn_noalloc(const float *a, const float *b, float *out, uint32_t m, uint32_t n, uint32_t k,
+                                              void *stream, char *err, size_t cap) {
+    using namespace jade;
+    if (err && cap) err[0] = '\0';
+    if (!a || !b || !out) return noalloc_fail(1, err, cap, "null operand pointer");
+    if (!m || !n || !k || m > INT_MAX || n > INT_MAX || k > INT_MAX || (uint64_t)m * k > INT_MAX || (uint64_t)m * n > INT_MAX)
+        return noalloc_fail(1, err, cap, "dimension must be in 1..=INT_MAX with products within 31-bit indexing");
+    if ((uint64_t)k * n > kNoAllocScratchFloats) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "K*N = %llu exceeds the %llu-element (16 MiB) static scratch of this entry point",
+                 (unsigned long long)k * n, (unsigned long long)kNoAllocScratchFloats);
+        return noalloc_fail(1, err, cap, msg);
+    }
+    if (k % 4 || (reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) % 16)
+        return noalloc_fail(1, err, cap, "TMA needs K to be a multiple of 4 and 16-byte aligned A and B");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return noalloc_fail(2, err, cap, "cudaGetDevice failed");
+    auto kernel = gemm_tc_kernel<4, 2, false, float, kEpiNone, false>;
+    NoAllocDevice *d = &g_noalloc_devices[dev];
+    {
+        // One-time set-up for this device (the current device): resolve the device
+        // addresses of the static arrays; host code never passes the symbols themselves.
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        if (!d->ready) {
+            if (cudaGetSymbolAddress(reinterpret_cast<void **>(&d->scratch), g_noalloc_scratch) != cudaSuccess ||
+                cudaGetSymbolAddress(reinterpret_cast<void **>(&d->err), g_noalloc_error) != cudaSuccess) {
+                cudaGetLastError();
+                return noalloc_fail(2, err, cap, "cudaGetSymbolAddress failed for the static scratch");
+            }
+            if (cudaMemset(d->err, 0, sizeof(int)) != cudaSuccess ||
+                cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess) {
+                cudaGetLastError();
+                return noalloc_fail(2, err, cap, "static scratch set-up failed");
+            }
+            d->ready = true;
+        }
+    }
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a, m, k, 32, BM) ||
+        !make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->scratch, n, k, 32, BN))
+        return noalloc_fail(2, err, cap, "cuTensorMapEncodeTiled failed");
+    GemmArgs args{};
+    args.out = out;
+    args.M = (int)m;
+    args.N = (int)n;
+    args.K = (int)k;
+    args.tiles_m = (int)((m + BM - 1) / BM);
+    args.tiles_n = (int)((n + BN - 1) / BN);
+    args.num_tiles = args.tiles_m * args.tiles_n;
+    args.kblocks = (int)((k + 31) / 32);
+    args.err = d->err;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // B [K,N] -> scratch [N,K]: the whole K*N region is rewritten, nothing needs clearing.
+    transpose_f32<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, st>>>(b, d->scratch, (int)k, (int)n);
+    kernel<<<std::min(args.num_tiles, d->sm_count), kThreads, kSmemBytes, st>>>(ma, mb, args);
+    cudaError_t status = cudaGetLastError();
+    if (status == cudaSuccess) status = cudaStreamSynchronize(st);
+    if (status != cudaSuccess) return noalloc_fail(2, err, cap, cudaGetErrorString(status));
+    int code = 0;
+    if (cudaMemcpy(&code, d->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return noalloc_fail(2, err, cap, "error word read failed");
+    if (code) {
+        cudaMemset(d->err, 0, sizeof(int));  // the word must start at zero for the next call
+        return noalloc_fail(4, err, cap, "device-side bounded wait expired in the TF32 GEMM");
+    }
+    return 0;
+}

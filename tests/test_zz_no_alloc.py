@@ -1,0 +1,66 @@
+"""The allocation-free TF32 GEMM entry point (jr_gemm_tf32_kn_noalloc).
+
+It exists for callers that cannot allocate device memory at call time (a host
+framework that owns every device allocation through its own pool, or a
+latency-critical loop where cudaMalloc's implicit synchronisation is not
+acceptable); its scratch is a static 16 MiB array inside the library. This test
+calls it through the C ABI twice in a row and checks each result against the
+compiled entry point (jr_compile + jr_execute2 of the same GEMM spec), within
+this suite's TF32 tolerance (src/validation.rs:35-91 form, reduced-precision
+coefficient 0.0012). The file name makes pytest collect it last.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import jade_compute_b200 as jc
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def noalloc_fn():
+    f = jc.lib().jr_gemm_tf32_kn_noalloc
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
+                  ctypes.c_uint32, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    f.restype = ctypes.c_int
+    return f
+
+
+def test_noalloc_matches_compiled_entry_point_twice():
+    f = noalloc_fn()
+    rt = jc.Runtime(0)
+    try:
+        for call, (m, n, k) in enumerate([(384, 1024, 2048), (200, 300, 136)]):
+            a, b = rt.alloc(m * k, "tf32"), rt.alloc(k * n, "tf32")
+            rt.fill(a, "uniform", seed=40 + call, stream=0, lo=-1.0, hi=1.0)
+            rt.fill(b, "uniform", seed=40 + call, stream=1, lo=-1.0, hi=1.0)
+            ref_out, out = rt.alloc(m * n), rt.alloc(m * n)
+            kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": "tf32"})
+            rt.execute([(kern, [a, b, ref_out])])
+            err = ctypes.create_string_buffer(256)
+            rc = f(a.ptr, b.ptr, out.ptr, m, n, k, None, err, 256)
+            assert rc == 0, err.value
+            got, want = rt.download(out), rt.download(ref_out)
+            af, bf = rt.download(a), rt.download(b)
+            rc1, v = O.validation_check(m, n, k, af, bf, got, budget=1 << 14, fp16=True)
+            assert rc1 == 0, v.max_scaled_error
+            rc2, r = O.compare(got, want.astype(np.float64), 1e-4, 1e-4)
+            assert rc2 == 0, r.max_abs_error
+    finally:
+        rt.close()
+
+
+def test_noalloc_rejects_oversized_and_unaligned():
+    f = noalloc_fn()
+    rt = jc.Runtime(0)
+    try:
+        a, b, c = rt.alloc(16), rt.alloc(16), rt.alloc(16)
+        err = ctypes.create_string_buffer(256)
+        assert f(a.ptr, b.ptr, c.ptr, 1, 4096, 4096, None, err, 256) == 1  # k*n = 16 Mi > 4 Mi elements
+        assert b"static scratch" in err.value
+        assert f(a.ptr, b.ptr, c.ptr, 4, 4, 3, None, err, 256) == 1  # k not a multiple of 4
+        assert f(None, b.ptr, c.ptr, 4, 4, 4, None, err, 256) == 1
+    finally:
+        rt.close()
