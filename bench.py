@@ -12,9 +12,11 @@ Contract (one JSON line on rank 0):
              measured dense BF16 peak; traffic from the committed ncu summary.
   cpu_baseline  the FP64 oracle (the reference's CPU attention restated,
              metal_lab.rs:33-73) on a bounded sample of rows, all host threads.
-  components GEMM 8192^3 BF16 (BASELINE targets), non-causal attention.
+  components GEMM 8192^3 BF16 split by output columns over the ranks, the
+             residual MLP block (tensor parallel with one
+             NCCL all-reduce), non-causal attention.
 Multi-GPU: one process per GPU (torchrun); each rank runs its own batch x head
-shard (weak scaling, no collective on the data path).
+shard of the headline attention (weak scaling, no collective on the data path).
 
 --impl reference times the reference's CPU implementation of the path (the
 oracle port) on the host cores instead and prints the same metric.
@@ -110,25 +112,14 @@ class ClockSampler:
 
 
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
-        return dist, world, rank, local
-    return None, 1, 0, 0
+    from jade_compute_b200 import parallel
+    rank, world, local = parallel.env_ranks()
+    return parallel.init_process_group(timeout_s=300), world, rank, local
 
 
 def reduce_max(dist, x):
-    if dist is None:
-        return x
-    import torch
-    t = torch.tensor([x], dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from jade_compute_b200 import parallel
+    return parallel.max_over_ranks(dist, x)
 
 
 def barrier(dist):
@@ -165,9 +156,8 @@ def cpu_attention_sample(seconds, threads, seed=0):
 
 
 def run_reference(args):
-    dist, world, rank, _ = dist_setup()
-    if rank != 0:
-        return 0
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0  # under torchrun only rank 0 times the host implementation
     from oracle import oracle as O
     threads = O.max_threads()
     per_step = max(1.0, min(10.0, 60.0 / max(args.steps + args.warmup, 1)))
@@ -206,19 +196,58 @@ def attention_bench(rt, jc, steps, warmup, causal, batch):
     return jobs, attn, (q, k, v, o), flush_buf
 
 
-def gemm_bench(rt, steps, warmup, m=8192):
-    a, b, c = rt.alloc(m * m, "bf16"), rt.alloc(m * m, "bf16"), rt.alloc(m * m, "bf16")
+def gemm_bench(rt, dist, world, steps, warmup, m=8192):
+    """One m^3 BF16 GEMM split by output columns over the ranks (strong scaling):
+    rank r computes C[:, cols_r] = A . B[:, cols_r] with B stored [N, K] per shard."""
+    from jade_compute_b200 import parallel
+    rank = dist.get_rank() if dist is not None else 0
+    cols = parallel.split_range(m, world, rank)
+    n = len(cols)
+    a, b, c = rt.alloc(m * m, "bf16"), rt.alloc(n * m, "bf16"), rt.alloc(m * n, "bf16")
     rt.fill(a, "uniform", seed=5, stream=0, lo=-1, hi=1)
-    rt.fill(b, "uniform", seed=5, stream=1, lo=-1, hi=1)
-    g = rt.compile({"op": "gemm", "m": m, "n": m, "k": m, "tiled": True, "dtype": "bf16", "out_dtype": "bf16"})
+    rt.fill(b, "uniform", seed=5, stream=1 + rank, lo=-1, hi=1)
+    layout = "kn" if world == 1 else "nk"
+    g = rt.compile({"op": "gemm", "m": m, "n": n, "k": m, "tiled": True, "dtype": "bf16", "out_dtype": "bf16",
+                    "b_layout": layout})
     rt.execute([(g, [a, b, c])], repeats=max(warmup, 3))
+    barrier(dist)
     t = rt.execute([(g, [a, b, c])], repeats=steps, per_job=True)
-    ms = t.job_ms[0] / steps
+    ms = reduce_max(dist, t.job_ms[0] / steps)
     tflops = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
     for x in (a, b, c):
         x.free()
-    return {"workload": f"GEMM {m}^3 BF16 in, FP32 accumulate, BF16 out (BASELINE configs[4])", "value": tflops,
-            "unit": "TFLOP/s", "ms_per_step": ms, "impl": g.info.get("impl")}
+    return {"workload": f"GEMM {m}^3 BF16 in, FP32 accumulate, BF16 out (BASELINE configs[4]), N-column shards",
+            "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
+            "impl": g.info.get("impl")}
+
+
+def mlp_bench(rt, dist, world, steps, warmup, peaks):
+    """T=8192, d=4096, ffn=14336 residual MLP, tensor parallel
+    over the ranks with one NCCL all-reduce after the down projection."""
+    from jade_compute_b200 import parallel
+    from jade_compute_b200.mlp import ResidualMLP
+    T, d, ffn = 8192, 4096, 14336
+    rank = dist.get_rank() if dist is not None else 0
+    if world > 1:
+        parallel.init_comm(rt, dist, timeout_ms=120000)
+    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank)
+    mlp.fill_synthetic(seed=11)
+    jobs = mlp.jobs()
+    rt.execute(jobs, repeats=max(warmup, 3))
+    barrier(dist)
+    t = rt.execute(jobs, repeats=steps, per_job=True)
+    ms = reduce_max(dist, t.gpu_ms / steps)
+    flops = 6.0 * T * d * ffn
+    per_gpu_tflops = flops / world / (ms * 1e-3) / 1e12
+    out = {"workload": f"residual MLP block T={T} d={d} ffn={ffn} BF16 (BASELINE configs[3]), tensor parallel x{world}",
+           "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
+           "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": [x / steps for x in t.job_ms],
+           "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
+                        "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
+           "kernels": [k.info.get("impl") for k, _ in jobs]}
+    if world > 1:
+        rt.comm_destroy()
+    return out
 
 
 def run_ours(args):
@@ -254,7 +283,8 @@ def run_ours(args):
         e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
         components = []
         if not args.quick:
-            components.append(gemm_bench(rt, max(5, min(args.steps, 20)), args.warmup))
+            components.append(gemm_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup))
+            components.append(mlp_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks))
             jobs_f, attn_f, bufs_f, fb = attention_bench(rt, jc, args.steps, args.warmup, False, B)
             tf = rt.execute(jobs_f, repeats=max(5, min(args.steps, 50)), per_job=True)
             ms_f = tf.job_ms[1] / max(5, min(args.steps, 50))

@@ -31,7 +31,7 @@
 namespace jade {
 namespace {
 
-constexpr int kBQ = 128, kBK = 128, kSoftWarps = 8, kThreads = (2 + kSoftWarps) * 32;
+constexpr int kBQ = 128, kBK = 128, kSoftWarps = 8, kThreads = (2 + kSoftWarps) * 32, kFirstSoftWarp = 2;
 
 template <int D>
 struct AttnLayout {
@@ -178,15 +178,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j + 1 < n_kv && !(ok = issue_s(j + 1))) break;
                 const int st = j & 1;
                 if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort_flag, err, kErrWaitTmaFull)) break;
+                // P_j is in shared memory and O has been rescaled to the new row
+                // maxima by the softmax warps before they arrive on p_full.
                 if (!mbar_wait(p_full, j & 1, abort_flag, err, kErrWaitProb)) break;
-                if (!mbar_wait(o_empty, (j & 1) ^ 1, abort_flag, err, kErrWaitPv)) break;
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + L::kV + st * L::kTile);
 #pragma unroll
                 for (int t = 0; t < kBK / 16; ++t) {
                     const uint64_t a = sdesc_sw128(sp + (t >> 2) * L::kChunk + (t & 3) * 32, 16, 1024);
                     const uint64_t b = sdesc_sw128(sv + t * 16 * 128, L::kChunk, 1024);
-                    umma<false>(tmem_o, a, b, kIdescO, t != 0);
+                    umma<false>(tmem_o, a, b, kIdescO, (j | t) != 0);
                 }
                 umma_commit(&v_empty[st]);
                 umma_commit(o_full);
@@ -194,9 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(mma_done);
             mbar_wait_drain(mma_done, 0, err);
         }
-    } else {
+    } else if (warp >= kFirstSoftWarp) {
         // ----------------------------------------------------- softmax warps
-        const int sw = warp - 2;               // 0..7
+        const int sw = warp - kFirstSoftWarp;  // 0..7
         const int quarter = warp & 3;          // TMEM lane quarter
         const int half = sw >> 2;              // column half
         const int row = quarter * 32 + lane;   // query row within the tile
@@ -220,34 +221,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             return other;
         };
 
-        float o_acc[kHalfCols];
-#pragma unroll
-        for (int i = 0; i < kHalfCols; ++i) o_acc[i] = 0.0f;
-        float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
+        float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
         int j = 0;
         for (; j < n_kv; ++j) {
             const int st = j & 1;
-            // ---- scores S_j (this thread's 64 columns)
+            // ---- scores S_j (this thread's 64 columns of its row)
             ok = mbar_wait(&s_full[st], (j >> 1) & 1, abort_flag, err, kErrWaitScore);
             ok = __all_sync(0xffffffffu, ok);
             float s[64];
             float pmax = -INFINITY;
             if (ok) {
                 tc_fence_after();
-                uint32_t r0[32], r1[32];
-                tmem_ld32(tmem_s[st] + lane_off + half * 64, r0);
-                tmem_ld32(tmem_s[st] + lane_off + half * 64 + 32, r1);
+                tmem_ld32f(tmem_s[st] + lane_off + half * 64, s);
+                tmem_ld32f(tmem_s[st] + lane_off + half * 64 + 32, s + 32);
                 tmem_wait_ld();
                 tc_fence_before();
                 mbar_arrive(&s_empty[st]);
                 const int k0 = j * kBK + half * 64;
                 const bool need_mask = (args.causal && j == qt) || (j * kBK + kBK > args.seq);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    s[i] = __uint_as_float(r0[i]) * args.scale_log2;
-                    s[32 + i] = __uint_as_float(r1[i]) * args.scale_log2;
-                }
+                for (int i = 0; i < 64; ++i) s[i] *= args.scale_log2;
                 if (need_mask) {
 #pragma unroll
                     for (int i = 0; i < 64; ++i) {
@@ -270,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 psum += s[i];
             }
             l_run = l_run * alpha + psum;
-            // ---- P_j may overwrite P_{j-1} once P_{j-1} V_{j-1} is done
+            // ---- P_{j-1} V_{j-1} must be done before P and O are touched
             if (j > 0) {
                 ok = mbar_wait(o_full, (j - 1) & 1, abort_flag, err, kErrWaitPv);
                 (void)exchange(0.0f, ok);
@@ -289,57 +283,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(pbuf) + row * 128 + ((g ^ (row & 7)) << 4)) = u;
             }
             fence_proxy_async();
-            mbar_arrive(p_full);
-            // ---- fold in O_{j-1} = P_{j-1} V_{j-1}
-            if (j > 0) {
+            // ---- rescale the running output O (in TMEM) to the new maxima; skipped
+            // when no row of this warp changed its maximum (alpha == 1 exactly)
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
                 tc_fence_after();
-#pragma unroll
+#pragma unroll 1
                 for (int c = 0; c < kHalfCols; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem_o + lane_off + half * kHalfCols + c, r);
+                    float r[32];
+                    const uint32_t ta = tmem_o + lane_off + half * kHalfCols + c;
+                    tmem_ld32f(ta, r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o_acc[c + i] = fmaf(o_acc[c + i], alpha_prev, __uint_as_float(r[i]));
+                    for (int i = 0; i < 32; ++i) r[i] *= alpha;
+                    tmem_st32f(ta, r);
                 }
-                tc_fence_before();
-                mbar_arrive(o_empty);
+                tmem_wait_st();
             }
-            alpha_prev = alpha;
+            tc_fence_before();
+            mbar_arrive(p_full);
         }
         if (ok && j == n_kv) {
             ok = mbar_wait(o_full, (n_kv - 1) & 1, abort_flag, err, kErrWaitPv);
             ok = __all_sync(0xffffffffu, ok);
+            const float other_l = exchange(l_run, ok);
             if (ok) {
                 tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < kHalfCols; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem_o + lane_off + half * kHalfCols + c, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o_acc[c + i] = fmaf(o_acc[c + i], alpha_prev, __uint_as_float(r[i]));
-                }
-            }
-            const float other_l = exchange(l_run, ok);
-            if (ok && q < args.seq) {
                 const float inv = 1.0f / (l_run + other_l);
                 TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * D + half * kHalfCols;
+#pragma unroll 1
+                for (int c = 0; c < kHalfCols; c += 32) {
+                    float r[32];
+                    tmem_ld32f(tmem_o + lane_off + half * kHalfCols + c, r);
+                    tmem_wait_ld();
+                    if (q < args.seq) {
 #pragma unroll
-                for (int c = 0; c < kHalfCols; c += 8) {
-                    if constexpr (std::is_same<TOut, float>::value) {
-                        *reinterpret_cast<float4 *>(o + c) = make_float4(o_acc[c] * inv, o_acc[c + 1] * inv, o_acc[c + 2] * inv, o_acc[c + 3] * inv);
-                        *reinterpret_cast<float4 *>(o + c + 4) =
-                            make_float4(o_acc[c + 4] * inv, o_acc[c + 5] * inv, o_acc[c + 6] * inv, o_acc[c + 7] * inv);
-                    } else {
-                        uint4 u;
-                        if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
-                            u.x = pack_bf16(o_acc[c] * inv, o_acc[c + 1] * inv); u.y = pack_bf16(o_acc[c + 2] * inv, o_acc[c + 3] * inv);
-                            u.z = pack_bf16(o_acc[c + 4] * inv, o_acc[c + 5] * inv); u.w = pack_bf16(o_acc[c + 6] * inv, o_acc[c + 7] * inv);
-                        } else {
-                            u.x = pack_f16(o_acc[c] * inv, o_acc[c + 1] * inv); u.y = pack_f16(o_acc[c + 2] * inv, o_acc[c + 3] * inv);
-                            u.z = pack_f16(o_acc[c + 4] * inv, o_acc[c + 5] * inv); u.w = pack_f16(o_acc[c + 6] * inv, o_acc[c + 7] * inv);
+                        for (int e = 0; e < 32; e += 8) {
+                            if constexpr (std::is_same<TOut, float>::value) {
+                                *reinterpret_cast<float4 *>(o + c + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
+                                *reinterpret_cast<float4 *>(o + c + e + 4) =
+                                    make_float4(r[e + 4] * inv, r[e + 5] * inv, r[e + 6] * inv, r[e + 7] * inv);
+                            } else {
+                                uint4 u;
+                                if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
+                                    u.x = pack_bf16(r[e] * inv, r[e + 1] * inv); u.y = pack_bf16(r[e + 2] * inv, r[e + 3] * inv);
+                                    u.z = pack_bf16(r[e + 4] * inv, r[e + 5] * inv); u.w = pack_bf16(r[e + 6] * inv, r[e + 7] * inv);
+                                } else {
+                                    u.x = pack_f16(r[e] * inv, r[e + 1] * inv); u.y = pack_f16(r[e + 2] * inv, r[e + 3] * inv);
+                                    u.z = pack_f16(r[e + 4] * inv, r[e + 5] * inv); u.w = pack_f16(r[e + 6] * inv, r[e + 7] * inv);
+                                }
+                                *reinterpret_cast<uint4 *>(o + c + e) = u;
+                            }
                         }
-                        *reinterpret_cast<uint4 *>(o + c) = u;
                     }
                 }
             }
@@ -383,6 +377,7 @@ LaunchFn attn_launch(Context *ctx, const Spec &s) {
     auto kernel = attention_tc_kernel<D, TIn, TOut>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem) != cudaSuccess)
         throw IrError("cannot reserve shared memory for the tcgen05 attention");
+
     const CUtensorMapDataType dt = std::is_same<TIn, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     AttnArgs base{};
     base.seq = (int)s.seq;
