@@ -221,6 +221,57 @@ def gemm_bench(rt, dist, world, steps, warmup, m=8192):
             "impl": g.info.get("impl")}
 
 
+def row_benches(rt, steps, warmup, peaks):
+    """RMSNorm and softmax on 16384 x 8192 (FP32 and BF16,
+    RMSNorm eps 1e-6, weight U[0.5,1.5], softmax logits N(0,1)*4), and the IR
+    expression max(2.5x+y, 0) over 2^28 FP32 elements. HBM-bound: algorithmic
+    bytes = one read of the input(s) + one write of the output (+ the weight)."""
+    R, C, n_expr = 16384, 8192, 1 << 28
+    out = []
+    flush_buf = rt.alloc_bytes(256 << 20)
+    flush = rt.compile({"op": "l2_flush", "bytes": 256 << 20})
+    for dtype in ("fp32", "bf16"):
+        sz = 4 if dtype == "fp32" else 2
+        x, y, w = rt.alloc(R * C, dtype), rt.alloc(R * C, dtype), rt.alloc(C, dtype)
+        rt.fill(x, "normal", seed=9, stream=0, lo=0.0, hi=4.0)
+        rt.fill(w, "uniform", seed=9, stream=1, lo=0.5, hi=1.5)
+        for op, spec, bufs, nbytes in (
+                ("rms_norm", {"op": "rms_norm", "rows": R, "cols": C, "epsilon": 1e-6, "dtype": dtype}, [x, w, y],
+                 2 * R * C * sz + C * sz),
+                ("softmax", {"op": "softmax", "rows": R, "cols": C, "dtype": dtype}, [x, y], 2 * R * C * sz)):
+            k = rt.compile(spec)
+            jobs = [(flush, [flush_buf]), (k, bufs)]
+            rt.execute(jobs, repeats=max(warmup, 3))
+            t = rt.execute(jobs, repeats=steps, per_job=True)
+            ms = t.job_ms[1] / steps
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out.append({"workload": f"{op} {R}x{C} {dtype} (BASELINE configs[2])", "value": gbs, "unit": "GB/s",
+                        "ms_per_step": ms, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                                                        "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]},
+                        "impl": k.info.get("impl")})
+        for b in (x, y, w):
+            b.free()
+    a, b, c = rt.alloc(n_expr), rt.alloc(n_expr), rt.alloc(n_expr)
+    rt.fill(a, "uniform", seed=10, stream=0, lo=-1, hi=1)
+    rt.fill(b, "uniform", seed=10, stream=1, lo=-1, hi=1)
+    expr = {"kind": "maximum", "left": {"kind": "add", "left": {"kind": "multiply", "left": {"kind": "input", "binding": 0},
+                                                               "right": {"kind": "constant", "value": 2.5}},
+                                        "right": {"kind": "input", "binding": 1}},
+            "right": {"kind": "constant", "value": 0.0}}
+    k = rt.compile({"op": "elementwise", "len": n_expr, "inputs": 2, "expression": expr})
+    jobs = [(flush, [flush_buf]), (k, [a, b, c])]
+    rt.execute(jobs, repeats=max(warmup, 3))
+    t = rt.execute(jobs, repeats=steps, per_job=True)
+    ms = t.job_ms[1] / steps
+    gbs = 3 * 4 * n_expr / (ms * 1e-3) / 1e9
+    out.append({"workload": "elementwise max(2.5x+y,0) over 2^28 fp32 (BASELINE configs[2])", "value": gbs, "unit": "GB/s",
+                "ms_per_step": ms, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                                "frac": gbs / peaks["hbm_gbs"]}, "impl": k.info.get("impl")})
+    for x in (a, b, c, flush_buf):
+        x.free()
+    return out
+
+
 def mlp_bench(rt, dist, world, steps, warmup, peaks):
     """T=8192, d=4096, ffn=14336 residual MLP, tensor parallel
     over the ranks with one NCCL all-reduce after the down projection."""
@@ -285,6 +336,7 @@ def run_ours(args):
         if not args.quick:
             components.append(gemm_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup))
             components.append(mlp_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks))
+            components.extend(row_benches(rt, max(5, min(args.steps, 20)), args.warmup, peaks))
             jobs_f, attn_f, bufs_f, fb = attention_bench(rt, jc, args.steps, args.warmup, False, B)
             tf = rt.execute(jobs_f, repeats=max(5, min(args.steps, 50)), per_job=True)
             ms_f = tf.job_ms[1] / max(5, min(args.steps, 50))
