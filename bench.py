@@ -177,7 +177,7 @@ def run_reference(args):
                        "global_batch": B, "seq_len": S, "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": descs[0]},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit_line(line)
     return 0
 
 
@@ -301,7 +301,39 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks):
     return out
 
 
+def run_only(args):
+    """One workload alone (for ncu captures of a single kernel family): prints
+    that workload's measurement as the JSON line."""
+    dist, world, rank, local = dist_setup()
+    import jade_compute_b200 as jc
+    peaks = load_peaks()
+    rt = jc.Runtime(local)
+    try:
+        w = args.only
+        if w in ("attention", "attention_full"):
+            jobs, attn, _, _ = attention_bench(rt, jc, args.steps, args.warmup, w == "attention", B)
+            t = rt.execute(jobs, repeats=args.steps, per_job=True)
+            ms = t.job_ms[1] / args.steps
+            f = causal_flops(B, H, S, D) if w == "attention" else full_flops(B, H, S, D)
+            res = {"workload": w, "value": f / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "impl": attn.info.get("impl")}
+        elif w == "gemm":
+            res = gemm_bench(rt, dist, world, args.steps, args.warmup)
+        elif w == "mlp":
+            res = mlp_bench(rt, dist, world, args.steps, args.warmup, peaks)
+        elif w == "rows":
+            res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks)}
+        else:
+            raise SystemExit(f"unknown workload {w}")
+        if rank == 0:
+            emit_line(res)
+    finally:
+        rt.close()
+    return 0
+
+
 def run_ours(args):
+    if args.only:
+        return run_only(args)
     dist, world, rank, local = dist_setup()
     import jade_compute_b200 as jc
     peaks = load_peaks()
@@ -371,7 +403,7 @@ def run_ours(args):
             "components": components,
         }
         if rank == 0:
-            print(json.dumps(line))
+            emit_line(line)
     finally:
         rt.close()
     if dist is not None:
@@ -381,6 +413,26 @@ def run_ours(args):
 
 
 def main():
+    # Native libraries (NCCL's version banner, driver messages) may write to fd 1;
+    # route fd 1 to stderr while working so stdout carries exactly one JSON line.
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(os.dup(2), "w")
+    try:
+        return _main(out_fd)
+    finally:
+        sys.stdout.flush()
+
+
+def emit_line(line):
+    os.write(_OUT_FD[0], (json.dumps(line) + "\n").encode())
+
+
+_OUT_FD = [1]
+
+
+def _main(out_fd):
+    _OUT_FD[0] = out_fd
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -389,6 +441,8 @@ def main():
     ap.add_argument("--quick", action="store_true", help="headline only, no components")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "mlp", "rows"], default=None,
+                    help="run one workload alone (profiling), printing its own measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

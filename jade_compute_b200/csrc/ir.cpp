@@ -101,20 +101,6 @@ void validate_expr(const Expr &e, uint32_t inputs, size_t depth, size_t &nodes) 
     }
 }
 
-// ir.rs:111-137 (CoreX dialect)
-std::string expr_code_corex(const Expr &e) {
-    switch (e.kind) {
-        case Expr::Input: return "input" + std::to_string(e.binding) + "[i]";
-        case Expr::Constant: return rust_lower_exp_f32(e.value) + "f";
-        case Expr::Add: return "(" + expr_code_corex(*e.left) + "+" + expr_code_corex(*e.right) + ")";
-        case Expr::Multiply: return "(" + expr_code_corex(*e.left) + "*" + expr_code_corex(*e.right) + ")";
-        case Expr::Maximum: return "fmaxf(" + expr_code_corex(*e.left) + "," + expr_code_corex(*e.right) + ")";
-        case Expr::Negate: return "(-" + expr_code_corex(*e.left) + ")";
-        case Expr::Exp: return "expf(" + expr_code_corex(*e.left) + ")";
-    }
-    return "";
-}
-
 void dim(uint32_t v) { ensure(v > 0 && v <= (uint32_t)INT_MAX, "dimension must be in 1..=INT_MAX"); }
 void matrix(uint64_t x, uint64_t y) {
     ensure(x > 0 && x <= (uint64_t)INT_MAX && y > 0 && y <= (uint64_t)INT_MAX, "dimension must be in 1..=INT_MAX");
@@ -478,75 +464,105 @@ Launch launch(const Spec &s) {  // ir.rs:368-420 (reference geometry of the emit
     }
 }
 
-std::string corex_source(const Spec &s) {  // ir.rs:450-575
-    ensure(!is_metal_specific(s), std::string(spec_name(s)) + " is a Metal-only operation; CoreX lowering is not implemented");
+namespace {
+
+// The two text dialects of ir.rs:461-464: CoreX (CUDA C++) and Metal Shading Language.
+struct Dialect {
+    bool metal;
+    const char *header, *signature, *prefix, *shared, *barrier, *exponential, *rsqrt_fn, *maximum, *fused;
+};
+const Dialect kCorex{false, "#include <cuda_runtime.h>\n#include <math.h>\n", "__global__ void jade_main",
+                     "    const uint3 gid = make_uint3(blockIdx.x*blockDim.x+threadIdx.x, blockIdx.y*blockDim.y+threadIdx.y, 0);\n"
+                     "    const uint3 tid = threadIdx;\n"
+                     "    const uint3 group = blockIdx;\n",
+                     "__shared__", "__syncthreads();", "expf", "rsqrtf", "fmaxf", "fmaf"};
+const Dialect kMetal{true, "#include <metal_stdlib>\nusing namespace metal;\n", "kernel void jade_main", "", "threadgroup",
+                     "threadgroup_barrier(mem_flags::mem_threadgroup);", "exp", "rsqrt", "fmax", "fma"};
+
+// ir.rs:111-137
+std::string expr_code(const Expr &e, const Dialect &d) {
+    switch (e.kind) {
+        case Expr::Input: return "input" + std::to_string(e.binding) + "[i]";
+        case Expr::Constant: return rust_lower_exp_f32(e.value) + "f";
+        case Expr::Add: return "(" + expr_code(*e.left, d) + "+" + expr_code(*e.right, d) + ")";
+        case Expr::Multiply: return "(" + expr_code(*e.left, d) + "*" + expr_code(*e.right, d) + ")";
+        case Expr::Maximum: return std::string(d.maximum) + "(" + expr_code(*e.left, d) + "," + expr_code(*e.right, d) + ")";
+        case Expr::Negate: return "(-" + expr_code(*e.left, d) + ")";
+        case Expr::Exp: return std::string(d.exponential) + "(" + expr_code(*e.left, d) + ")";
+    }
+    return "";
+}
+
+// ir.rs:458-575
+std::string source(const Spec &s, const Dialect &d) {
     validate(s);
-    ensure(!s.extended(), std::string(spec_name(s)) + " uses backend extensions; the CoreX dialect covers reference FP32 operations only");
+    ensure(!s.extended(), std::string(spec_name(s)) + " uses backend extensions; the emitted dialects cover reference FP32 operations only");
     const auto bs = bindings(s);
     std::string args;
     for (size_t i = 0; i < bs.size(); ++i) {
         if (i) args += ", ";
-        args += std::string(bs[i].write ? "" : "const ") + "float* " + bs[i].name;
+        const std::string q = bs[i].write ? "" : "const ";
+        if (d.metal) args += "device " + q + "float* " + bs[i].name + " [[buffer(" + std::to_string(i) + ")]]";
+        else args += q + "float* " + bs[i].name;
     }
-    const std::string prefix =
-        "    const uint3 gid = make_uint3(blockIdx.x*blockDim.x+threadIdx.x, blockIdx.y*blockDim.y+threadIdx.y, 0);\n"
-        "    const uint3 tid = threadIdx;\n"
-        "    const uint3 group = blockIdx;\n";
+    if (d.metal)
+        args += ", uint3 gid [[thread_position_in_grid]], uint3 tid [[thread_position_in_threadgroup]], uint3 group [[threadgroup_position_in_grid]]";
+    const std::string sh = d.shared, bar = d.barrier, ex = d.exponential, mx = d.maximum, fu = d.fused;
     std::string body;
     switch (s.op) {
         case Op::Elementwise:
-            body = "    const unsigned i=gid.x;\n    if(i<" + u(s.len) + ") out[i]=" + expr_code_corex(*s.expression) + ";\n";
+            body = "    const unsigned i=gid.x;\n    if(i<" + u(s.len) + ") out[i]=" + expr_code(*s.expression, d) + ";\n";
             break;
         case Op::Axpy:
-            body = "    const unsigned i=gid.x;\n    if(i<" + u(s.len) + ") out[i]=fmaf(" + rust_lower_exp_f32(s.alpha) + "f,a[i],b[i]);\n";
+            body = "    const unsigned i=gid.x;\n    if(i<" + u(s.len) + ") out[i]=" + fu + "(" + rust_lower_exp_f32(s.alpha) + "f,a[i],b[i]);\n";
             break;
         case Op::Add: body = "    const unsigned i=gid.x;\n    if(i<" + u(s.len) + ") out[i]=a[i]+b[i];\n"; break;
         case Op::SwiGlu:
             body = "    const unsigned i=gid.x;\n    if(i<" + u(s.len) + ") {\n        const float v=gate[i];\n"
-                   "        const float e=expf(-fabs(v));\n"
+                   "        const float e=" + ex + "(-fabs(v));\n"
                    "        const float sigmoid=v>=0.0f?1.0f/(1.0f+e):e/(1.0f+e);\n"
                    "        out[i]=(v*sigmoid)*up[i];\n    }\n";
             break;
         case Op::RmsNorm: {
             const std::string c = std::to_string(s.cols);
-            body = "    __shared__ float partial[256];\n"
+            body = "    " + sh + " float partial[256];\n"
                    "    const unsigned row=group.x, lane=tid.x;\n"
                    "    float sum=0.0f;\n"
-                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) { float v=x[row*" + c + "u+c]; sum=fmaf(v,v,sum); }\n"
+                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) { float v=x[row*" + c + "u+c]; sum=" + fu + "(v,v,sum); }\n"
                    "    partial[lane]=sum;\n"
-                   "    __syncthreads();\n"
+                   "    " + bar + "\n"
                    "    for(unsigned step=128u;step>0u;step/=2u) {\n"
                    "        if(lane<step) partial[lane]+=partial[lane+step];\n"
-                   "        __syncthreads();\n"
+                   "        " + bar + "\n"
                    "    }\n"
-                   "    const float inv=rsqrtf(partial[0]/" + c + ".0f+" + rust_lower_exp_f32(s.epsilon) + "f);\n"
+                   "    const float inv=" + d.rsqrt_fn + "(partial[0]/" + c + ".0f+" + rust_lower_exp_f32(s.epsilon) + "f);\n"
                    "    for(unsigned c=lane;c<" + c + "u;c+=256u) out[row*" + c + "u+c]=x[row*" + c + "u+c]*inv*weight[c];\n";
             break;
         }
         case Op::Softmax: {
             const std::string c = std::to_string(s.cols);
-            body = "    __shared__ float partial[256];\n"
+            body = "    " + sh + " float partial[256];\n"
                    "    const unsigned row=group.x, lane=tid.x;\n"
                    "    float maxv=-INFINITY;\n"
-                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) maxv=fmaxf(maxv,x[row*" + c + "u+c]);\n"
+                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) maxv=" + mx + "(maxv,x[row*" + c + "u+c]);\n"
                    "    partial[lane]=maxv;\n"
-                   "    __syncthreads();\n"
+                   "    " + bar + "\n"
                    "    for(unsigned step=128u;step>0u;step/=2u) {\n"
-                   "        if(lane<step) partial[lane]=fmaxf(partial[lane],partial[lane+step]);\n"
-                   "        __syncthreads();\n"
+                   "        if(lane<step) partial[lane]=" + mx + "(partial[lane],partial[lane+step]);\n"
+                   "        " + bar + "\n"
                    "    }\n"
                    "    maxv=partial[0];\n"
-                   "    __syncthreads();\n"
+                   "    " + bar + "\n"
                    "    float sum=0.0f;\n"
-                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) sum+=expf(x[row*" + c + "u+c]-maxv);\n"
+                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) sum+=" + ex + "(x[row*" + c + "u+c]-maxv);\n"
                    "    partial[lane]=sum;\n"
-                   "    __syncthreads();\n"
+                   "    " + bar + "\n"
                    "    for(unsigned step=128u;step>0u;step/=2u) {\n"
                    "        if(lane<step) partial[lane]+=partial[lane+step];\n"
-                   "        __syncthreads();\n"
+                   "        " + bar + "\n"
                    "    }\n"
                    "    const float denom=partial[0];\n"
-                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) out[row*" + c + "u+c]=expf(x[row*" + c + "u+c]-maxv)/denom;\n";
+                   "    for(unsigned c=lane;c<" + c + "u;c+=256u) out[row*" + c + "u+c]=" + ex + "(x[row*" + c + "u+c]-maxv)/denom;\n";
             break;
         }
         case Op::Gemm: {
@@ -555,11 +571,11 @@ std::string corex_source(const Spec &s) {  // ir.rs:450-575
                 body = "    const unsigned row=gid.y,col=gid.x;\n"
                        "    if(row<" + m + "u && col<" + n + "u) {\n"
                        "        float sum=0.0f;\n"
-                       "        for(unsigned p=0u;p<" + k + "u;++p) sum=fmaf(a[row*" + k + "u+p],b[p*" + n + "u+col],sum);\n"
+                       "        for(unsigned p=0u;p<" + k + "u;++p) sum=" + fu + "(a[row*" + k + "u+p],b[p*" + n + "u+col],sum);\n"
                        "        out[row*" + n + "u+col]=sum;\n"
                        "    }\n";
             } else {
-                body = "    __shared__ float tile_a[512], tile_b[512];\n"
+                body = "    " + sh + " float tile_a[512], tile_b[512];\n"
                        "    const unsigned linear_thread=tid.y*8u+tid.x;\n"
                        "    const unsigned tile_row=group.y*32u, tile_col=group.x*32u;\n"
                        "    const unsigned local_row=tid.y*4u, local_col=tid.x*4u;\n"
@@ -572,14 +588,14 @@ std::string corex_source(const Spec &s) {  // ir.rs:450-575
                        "            tile_a[slot]=(ar<" + m + "u && ac<" + k + "u)?a[ar*" + k + "u+ac]:0.0f;\n"
                        "            tile_b[slot]=(br<" + k + "u && bc<" + n + "u)?b[br*" + n + "u+bc]:0.0f;\n"
                        "        }\n"
-                       "        __syncthreads();\n"
+                       "        " + bar + "\n"
                        "        for(unsigned p=0u;p<16u;++p) {\n"
                        "            for(unsigned r=0u;r<4u;++r) {\n"
                        "                const float av=tile_a[(local_row+r)*16u+p];\n"
-                       "                for(unsigned c=0u;c<4u;++c) acc[r][c]=fmaf(av,tile_b[p*32u+local_col+c],acc[r][c]);\n"
+                       "                for(unsigned c=0u;c<4u;++c) acc[r][c]=" + fu + "(av,tile_b[p*32u+local_col+c],acc[r][c]);\n"
                        "            }\n"
                        "        }\n"
-                       "        __syncthreads();\n"
+                       "        " + bar + "\n"
                        "    }\n"
                        "    for(unsigned r=0u;r<4u;++r) for(unsigned c=0u;c<4u;++c) {\n"
                        "        const unsigned row=tile_row+local_row+r, col=tile_col+local_col+c;\n"
@@ -588,22 +604,37 @@ std::string corex_source(const Spec &s) {  // ir.rs:450-575
             }
             break;
         }
-        default: bail("no CoreX lowering for this operation");
+        default: bail("Metal-specific operations use their own checked source emitters");
     }
-    std::string src = std::string("// Generated by Jade checked operation IR: ") + spec_name(s) + "\n" +
-                      "#include <cuda_runtime.h>\n#include <math.h>\n" + "__global__ void jade_main(" + args + ") {\n" + prefix + body + "}\n";
-    const Launch l = launch(s);
-    std::string casts;
-    for (size_t i = 0; i < bs.size(); ++i) {
-        if (i) casts += ",";
-        casts += std::string("static_cast<") + (bs[i].write ? "" : "const ") + "float*>(buffers[" + std::to_string(i) + "])";
+    std::string src = std::string("// Generated by Jade checked operation IR: ") + spec_name(s) + "\n" + d.header + d.signature + "(" + args +
+                      ") {\n" + d.prefix + body + "}\n";
+    if (!d.metal) {
+        const Launch l = launch(s);
+        std::string casts;
+        for (size_t i = 0; i < bs.size(); ++i) {
+            if (i) casts += ",";
+            casts += std::string("static_cast<") + (bs[i].write ? "" : "const ") + "float*>(buffers[" + std::to_string(i) + "])";
+        }
+        char head[256];
+        snprintf(head, sizeof head, "    jade_main<<<dim3(%u,%u,%u),dim3(%u,%u,%u),0,static_cast<cudaStream_t>(stream)>>>(",
+                 l.grid[0], l.grid[1], l.grid[2], l.block[0], l.block[1], l.block[2]);
+        src += "extern \"C\" int jade_generated_launch(void* stream, void** buffers) {\n" + std::string(head) + casts +
+               ");\n    return static_cast<int>(cudaGetLastError());\n}\n";
     }
-    char head[256];
-    snprintf(head, sizeof head, "    jade_main<<<dim3(%u,%u,%u),dim3(%u,%u,%u),0,static_cast<cudaStream_t>(stream)>>>(",
-             l.grid[0], l.grid[1], l.grid[2], l.block[0], l.block[1], l.block[2]);
-    src += "extern \"C\" int jade_generated_launch(void* stream, void** buffers) {\n" + std::string(head) + casts +
-           ");\n    return static_cast<int>(cudaGetLastError());\n}\n";
     return src;
+}
+
+}  // namespace
+
+std::string corex_source(const Spec &s) {  // ir.rs:450-457
+    ensure(!is_metal_specific(s), std::string(spec_name(s)) + " is a Metal-only operation; CoreX lowering is not implemented");
+    return source(s, kCorex);
+}
+
+std::string metal_source(const Spec &s) {  // ir.rs:421-449 for the operations whose MSL comes from source()
+    ensure(!is_metal_specific(s), std::string(spec_name(s)) +
+                                      " uses a Metal-specific source template (metal_simd.rs / metal_attention.rs), which this backend does not emit");
+    return source(s, kMetal);
 }
 
 std::string expr_cuda_code(const Expr &e, const std::vector<std::string> &names) {

@@ -99,6 +99,9 @@ void validate_bindings(const Spec &s, const std::vector<uint64_t> &lengths,
                        const std::vector<uint64_t> &ids);
 Launch launch(const Spec &s);
 std::string corex_source(const Spec &s);
+// Metal Shading Language text of the same templates (ir.rs:421-449) for the
+// reference operations emitted through source(); text only, never compiled here.
+std::string metal_source(const Spec &s);
 // sm_100a lowering of an elementwise expression: a vectorised grid-stride kernel
 // named jade_elementwise(const float* input0.., float* out, unsigned long long n).
 std::string cuda_elementwise_source(const Spec &s);

@@ -328,7 +328,8 @@ extern "C" int jr_spec_emit(const char *spec_json, const char *target, char *out
         std::string src;
         if (!strcmp(target, "corex")) src = jade::corex_source(s);
         else if (!strcmp(target, "cuda")) src = jade::cuda_elementwise_source(s);
-        else return fail(JR_EINVAL, err, cap, "unknown emit target `%s` (corex, cuda)", target);
+        else if (!strcmp(target, "metal")) src = jade::metal_source(s);
+        else return fail(JR_EINVAL, err, cap, "unknown emit target `%s` (corex, metal, cuda)", target);
         if (needed) *needed = src.size() + 1;
         return copy_out(src, out, out_cap, err, cap);
     })

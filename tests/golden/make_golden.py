@@ -2,7 +2,7 @@
 output (reports/generated-native/ in the reference tree: 19 cases of
 `jade-runtime emit-suite`, src/bin/jade-runtime.rs:218-244).
 
-Only digests and the small launch/binding records are stored, not the emitted
+Only digests (of the .cu, .metal and .json files) and the small launch/binding records are stored, not the emitted
 source text: the tests compare sha256 of this repository's emitter output with
 the reference's, byte for byte.
 
@@ -32,6 +32,7 @@ def main():
         cases.append({
             "case": name,
             "cu_sha256": sha(os.path.join(SRC, name + ".cu")),
+            "metal_sha256": sha(os.path.join(SRC, name + ".metal")),
             "spec_json_sha256": sha(os.path.join(SRC, name + ".json")),
             "launch": c["launch"],
             "bindings": c["bindings"],

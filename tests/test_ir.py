@@ -130,6 +130,8 @@ def test_corex_emitter_byte_exact(case):
     if HAS_REF:  # direct diff for a readable failure where the reference tree exists
         with open(os.path.join(REF_ROOT, "reports", "generated-native", name + ".cu")) as f:
             assert f.read() == text
+    metal = jc.emit(spec, "metal") + "\n"
+    assert hashlib.sha256(metal.encode()).hexdigest() == g["metal_sha256"], metal
     assert jc.spec_launch(spec) == g["launch"]
     b = [{k: x[k] for k in ("elements", "name", "write")} for x in jc.spec_bindings(spec)]
     assert b == g["bindings"]
