@@ -301,6 +301,53 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks):
     return out
 
 
+def sweep(rt, dist, world, rank, steps, warmup, peaks):
+    """BASELINE config 5 on this box: BF16 and TF32 square GEMMs M=N=K in
+    {1k..16k} split by output columns over the ranks, and causal attention B=8,
+    H=32, D=128, S in {4k, 8k, 16k} split by batch x head (B*H/world heads per rank)."""
+    from jade_compute_b200 import parallel
+    out = []
+    for dtype in ("bf16", "tf32"):
+        for m in (1024, 2048, 4096, 8192, 16384):
+            cols = parallel.split_range(m, world, rank)
+            n = len(cols)
+            a, b, c = rt.alloc(m * m, dtype), rt.alloc(n * m, dtype), rt.alloc(m * n, "fp32")
+            rt.fill(a, "uniform", seed=7, stream=0, lo=-1, hi=1)
+            rt.fill(b, "uniform", seed=7, stream=1 + rank, lo=-1, hi=1)
+            g = rt.compile({"op": "gemm", "m": m, "n": n, "k": m, "tiled": True, "dtype": dtype, "b_layout": "nk"})
+            reps = max(3, min(steps, int(2e13 / (2.0 * m ** 3)) + 1))
+            rt.execute([(g, [a, b, c])], repeats=max(warmup, 2))
+            barrier(dist)
+            t = rt.execute([(g, [a, b, c])], repeats=reps, per_job=True)
+            ms = reduce_max(dist, t.job_ms[0] / reps)
+            tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
+            out.append({"workload": f"GEMM {m}^3 {dtype} (FP32 out), N-split x{world}", "value": tf, "unit": "TFLOP/s",
+                        "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"], "impl": g.info.get("impl")})
+            for x in (a, b, c):
+                x.free()
+    Bs, Hs = 8, 32
+    for seq in (4096, 8192, 16384):
+        heads = parallel.split_range(Bs * Hs, world, rank)
+        nh = len(heads)
+        n = nh * seq * D
+        q, k, v, o = (rt.alloc(n, "bf16") for _ in range(4))
+        for i, buf in enumerate((q, k, v)):
+            rt.fill(buf, "normal", seed=8, stream=i + 4 * rank, lo=0.0, hi=1.0)
+        attn = rt.compile({"op": "attention_online", "heads": nh, "seq": seq, "dim": D, "causal": True, "dtype": "bf16"})
+        rt.execute([(attn, [q, k, v, o])], repeats=max(warmup, 2))
+        barrier(dist)
+        reps = max(3, min(steps, 20))
+        t = rt.execute([(attn, [q, k, v, o])], repeats=reps, per_job=True)
+        ms = reduce_max(dist, t.job_ms[0] / reps)
+        tf = causal_flops(Bs, Hs, seq, D) / (ms * 1e-3) / 1e12
+        out.append({"workload": f"causal attention B={Bs} H={Hs} S={seq} D={D} BF16, batch x head split x{world}",
+                    "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"],
+                    "impl": attn.info.get("impl")})
+        for x in (q, k, v, o):
+            x.free()
+    return out
+
+
 def run_only(args):
     """One workload alone (for ncu captures of a single kernel family): prints
     that workload's measurement as the JSON line."""
@@ -322,6 +369,8 @@ def run_only(args):
             res = mlp_bench(rt, dist, world, args.steps, args.warmup, peaks)
         elif w == "rows":
             res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks)}
+        elif w == "sweep":
+            res = {"workload": "sweep", "components": sweep(rt, dist, world, rank, args.steps, args.warmup, peaks)}
         else:
             raise SystemExit(f"unknown workload {w}")
         if rank == 0:
@@ -441,7 +490,7 @@ def _main(out_fd):
     ap.add_argument("--quick", action="store_true", help="headline only, no components")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "mlp", "rows"], default=None,
+    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "mlp", "rows", "sweep"], default=None,
                     help="run one workload alone (profiling), printing its own measurement")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -4,22 +4,26 @@
 // reference's online attention (src/runtime/metal_attention.rs:44-137, oracle
 // src/runtime/metal_lab.rs:33-73) extended to a batch dimension: Q/K/V/O are
 // [batch, heads, seq, dim] row-major, dim 64 or 128. Softmax statistics are
-// FP32; P is rounded to the input type for the P.V product; O accumulates in FP32.
+// FP32; P is rounded to the input type for P.V; O accumulates in FP32 in TMEM.
 //
-// One CTA owns 128 queries of one (batch, head):
-//   warp 0      TMA producer: Q once, then K_j / V_j into two-stage rings with
-//               separate K and V barriers (K_j's slot refills once S_j is done)
-//   warp 1      MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before O_j = P_j V_j, so
-//               the tensor core computes the next scores while softmax runs
-//   warps 2-9   softmax + correction + epilogue. Two warps share each 32-lane TMEM
-//               quarter (= 32 query rows) and split the 128 score columns and the
-//               D output columns; the pair exchanges row maxima through shared
-//               memory (named barrier per pair).
-// TMEM: S double buffer (2 x 128 columns) + P.V tile (D columns). The running
-// output stays in registers (64 FP32 per thread), rescaled by exp2(m_old-m_new).
-// Causal: key tiles above the diagonal are skipped; q-tiles are scheduled
-// heaviest first. Every wait is bounded and the abort decision is made
-// uniformly per warp pair so no thread is left at a barrier.
+// One CTA owns two 128-query tiles (A, B) of one (batch, head) and streams the
+// shared K/V tiles of 128 keys once for both:
+//   warp 0     TMA: Q_A, Q_B once; K_j, V_j into two-stage rings (separate K and
+//              V barriers: K_j's slot refills as soon as both S_A(j), S_B(j) are done)
+//   warp 1     MMA, in the order  S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ...
+//              so the tensor core works on one tile while the other tile's
+//              softmax runs (ping-pong). P_t(j) is read from TMEM (A operand).
+//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: one thread per
+//              query row (TMEM lane); pass 1 reads S_t(j) for the row maximum,
+//              pass 2 reads it again, writes P = exp2(S*scale - m) as 16-bit
+//              pairs over the first 64 columns of the same TMEM buffer.
+// TMEM: S_A | S_B | O_A | O_B (128 columns each). O is rescaled in place only
+// when a row maximum grows by more than 2^8 (until then P <= 256 is exact
+// enough in FP32 accumulation), so steady-state iterations never touch O.
+// When S_t(j) lands, P_t(j-1).V(j-1) has completed (both come from the MMA lane
+// in that order), so the rescale needs no extra wait.
+// Causal: tiles above the diagonal are skipped; the heaviest pairs go first.
+// Every wait is bounded; an abort makes each warp leave at a warp-uniform point.
 #include <cuda.h>
 
 #include <mutex>
@@ -31,36 +35,54 @@
 namespace jade {
 namespace {
 
-constexpr int kBQ = 128, kBK = 128, kSoftWarps = 8, kThreads = (2 + kSoftWarps) * 32, kFirstSoftWarp = 2;
+constexpr int kBQ = 128, kBK = 128, kThreads = 10 * 32;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when a row max grows by more than 2^8
 
 template <int D>
 struct AttnLayout {
-    static constexpr uint32_t kChunk = 128 * 128;              // 128 rows x 128 B (64 elements)
-    static constexpr uint32_t kTile = (D / 64) * kChunk;       // Q / K / V tile bytes
-    static constexpr uint32_t kQ = 0;
-    static constexpr uint32_t kK = kQ + kTile;                  // 2 stages
-    static constexpr uint32_t kV = kK + 2 * kTile;              // 2 stages
-    static constexpr uint32_t kP = kV + 2 * kTile;              // 128 x 128 (2 chunks)
-    static constexpr uint32_t kBar = kP + 2 * kChunk;
-    static constexpr uint32_t kXch = kBar + 256;                // pair exchange buffers
-    static constexpr uint32_t kEnd = kXch + 4 * 2 * 128 * 8;    // [slot 4][half 2][row 128] x (float, int)
-    static constexpr uint32_t kSmem = kEnd + 1024;
+    static constexpr uint32_t kChunk = 128 * 128;          // 128 rows x 128 B (64 elements)
+    static constexpr uint32_t kTile = (D / 64) * kChunk;   // Q / K / V tile bytes
+    static constexpr uint32_t kQ = 0;                       // Q_A, Q_B
+    static constexpr uint32_t kK = kQ + 2 * kTile;          // 2 stages
+    static constexpr uint32_t kV = kK + 2 * kTile;          // 2 stages
+    static constexpr uint32_t kBar = kV + 2 * kTile;
+    static constexpr uint32_t kSmem = kBar + 256 + 1024;
 };
 
 struct AttnArgs {
     void *out;
-    int seq, heads_total, nq_tiles, nkv_tiles, causal;
+    int seq, nq_tiles, npairs, nkv_tiles, causal;
     float scale_log2;
     int *err;
 };
 
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 32 lanes x 8 columns of 32-bit values from registers into TMEM.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+                 "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+// 32 lanes x 16 columns of 32-bit values from registers into TMEM.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 
 template <int D, typename TIn, typename TOut>
@@ -72,25 +94,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kIdescS = idesc_f32acc(kFmt, kFmt, false, false, kBQ, kBK);
     constexpr uint32_t kIdescO = idesc_f32acc(kFmt, kFmt, false, true, kBQ, D);
     constexpr int kDChunks = D / 64;
-    constexpr int kHalfCols = D / 2;  // output columns per softmax thread
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBar);
     uint64_t *q_full = bars + 0;
     uint64_t *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
-    uint64_t *s_full = bars + 9, *s_empty = bars + 11, *p_full = bars + 13, *o_full = bars + 14, *o_empty = bars + 15;
-    uint64_t *mma_done = bars + 16;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 17);
+    uint64_t *s_full = bars + 9, *p_full = bars + 11, *o_full = bars + 13;  // [tile]
+    uint64_t *mma_done = bars + 15;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    float *xch_v = reinterpret_cast<float *>(smem + L::kXch);
-    int *xch_ok = reinterpret_cast<int *>(smem + L::kXch + 4 * 2 * 128 * 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.x;
-    const int qt = args.nq_tiles - 1 - (int)blockIdx.y;  // heaviest causal tiles first
-    const int q0 = qt * kBQ;
-    const int n_kv = args.causal ? min(qt + 1, args.nkv_tiles) : args.nkv_tiles;
+    const int pair = args.npairs - 1 - (int)blockIdx.y;  // heaviest causal pairs first
+    int qt[2], nkv[2];
+    for (int t = 0; t < 2; ++t) {
+        qt[t] = 2 * pair + t;
+        nkv[t] = qt[t] >= args.nq_tiles ? 0 : (args.causal ? min(qt[t] + 1, args.nkv_tiles) : args.nkv_tiles);
+    }
+    const int nkv_max = max(nkv[0], nkv[1]);
     int *err = args.err;
 
     if (threadIdx.x == 0) {
@@ -98,11 +121,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < 2; ++s) {
             mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
             mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1);
-            mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], kSoftWarps * 32);
+            mbar_init(&s_full[s], 1); mbar_init(&p_full[s], 128); mbar_init(&o_full[s], 1);
         }
-        mbar_init(p_full, kSoftWarps * 32);
-        mbar_init(o_full, 1);
-        mbar_init(o_empty, kSoftWarps * 32);
         mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -117,19 +137,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tmem_s[2] = {tmem, tmem + 128};
-    const uint32_t tmem_o = tmem + 256;
+    const uint32_t tmem_o[2] = {tmem + 256, tmem + 384};
 
     if (warp == 0) {
         if (lane == 0) {  // ------------------------------------- TMA producer
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            bool k_issued[2] = {false, false}, v_issued[2] = {false, false}, q_issued = false;
+            bool k_issued[2] = {false, false}, v_issued[2] = {false, false};
             uint32_t k_last[2] = {0, 0}, v_last[2] = {0, 0};
-            mbar_arrive_expect_tx(q_full, L::kTile);
-            for (int c = 0; c < kDChunks; ++c) tma_load_3d(smem + L::kQ + c * L::kChunk, &tmQ, q_full, c * 64, q0, bh);
-            q_issued = true;
-            for (int j = 0; j < n_kv && !*abort_flag; ++j) {
+            const int ntiles = (nkv[0] > 0) + (nkv[1] > 0);
+            mbar_arrive_expect_tx(q_full, ntiles * L::kTile);
+            for (int t = 0; t < 2; ++t)
+                if (nkv[t] > 0)
+                    for (int c = 0; c < kDChunks; ++c)
+                        tma_load_3d(smem + L::kQ + t * L::kTile + c * L::kChunk, &tmQ, q_full, c * 64, qt[t] * kBQ, bh);
+            for (int j = 0; j < nkv_max && !*abort_flag; ++j) {
                 const int st = j & 1;
                 const uint32_t ph = (j >> 1) & 1;
                 if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
@@ -146,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 v_last[st] = ph;
             }
             if (*abort_flag) {
-                if (q_issued) mbar_wait_drain(q_full, 0, err);
+                if (ntiles) mbar_wait_drain(q_full, 0, err);
                 for (int s = 0; s < 2; ++s) {
                     if (k_issued[s]) mbar_wait_drain(&k_full[s], k_last[s], err);
                     if (v_issued[s]) mbar_wait_drain(&v_full[s], v_last[s], err);
@@ -155,172 +178,152 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ------------------------------------- MMA issuer
-            const uint32_t sq = smem_u32(smem + L::kQ), sp = smem_u32(smem + L::kP);
-            auto issue_s = [&](int j) -> bool {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&k_full[st], ph, abort_flag, err, kErrWaitTmaFull)) return false;
-                if (!mbar_wait(&s_empty[st], ph ^ 1, abort_flag, err, kErrWaitScore)) return false;
-                tc_fence_after();
-                const uint32_t sk = smem_u32(smem + L::kK + st * L::kTile);
+            const uint32_t sq0 = smem_u32(smem + L::kQ);
+            auto issue_s = [&](int t, int j) {
+                const uint32_t sq = sq0 + t * L::kTile, sk = smem_u32(smem + L::kK + (j & 1) * L::kTile);
 #pragma unroll
-                for (int t = 0; t < D / 16; ++t) {
-                    const uint32_t off = (t >> 2) * L::kChunk + (t & 3) * 32;
-                    umma<false>(tmem_s[st], sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), kIdescS, t != 0);
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint32_t off = (k >> 2) * L::kChunk + (k & 3) * 32;
+                    umma<false>(tmem_s[t], sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), kIdescS, k != 0);
                 }
-                umma_commit(&k_empty[st]);
-                umma_commit(&s_full[st]);
-                return true;
+                umma_commit(&s_full[t]);
             };
-            bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrWaitTmaFull);
-            if (ok) ok = issue_s(0);
-            for (int j = 0; ok && j < n_kv; ++j) {
-                if (j + 1 < n_kv && !(ok = issue_s(j + 1))) break;
-                const int st = j & 1;
-                if (!mbar_wait(&v_full[st], (j >> 1) & 1, abort_flag, err, kErrWaitTmaFull)) break;
-                // P_j is in shared memory and O has been rescaled to the new row
-                // maxima by the softmax warps before they arrive on p_full.
-                if (!mbar_wait(p_full, j & 1, abort_flag, err, kErrWaitProb)) break;
-                tc_fence_after();
-                const uint32_t sv = smem_u32(smem + L::kV + st * L::kTile);
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t sv = smem_u32(smem + L::kV + (j & 1) * L::kTile);
 #pragma unroll
-                for (int t = 0; t < kBK / 16; ++t) {
-                    const uint64_t a = sdesc_sw128(sp + (t >> 2) * L::kChunk + (t & 3) * 32, 16, 1024);
-                    const uint64_t b = sdesc_sw128(sv + t * 16 * 128, L::kChunk, 1024);
-                    umma<false>(tmem_o, a, b, kIdescO, (j | t) != 0);
+                for (int k = 0; k < kBK / 16; ++k)
+                    umma_ts(tmem_o[t], tmem_s[t] + k * 8, sdesc_sw128(sv + k * 16 * 128, L::kChunk, 1024), kIdescO, (j | k) != 0);
+                umma_commit(&o_full[t]);
+            };
+            bool ok = nkv_max > 0 && mbar_wait(q_full, 0, abort_flag, err, kErrWaitTmaFull);
+            if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrWaitTmaFull);
+            if (ok) {
+                tc_fence_after();
+                for (int t = 0; t < 2; ++t)
+                    if (nkv[t] > 0) issue_s(t, 0);
+                umma_commit(&k_empty[0]);
+            }
+            for (int j = 0; ok && j < nkv_max; ++j) {
+                const bool more = j + 1 < nkv_max;
+                bool k_ready = false;
+                if (!(ok = mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
+                for (int t = 0; t < 2 && ok; ++t) {
+                    if (j >= nkv[t]) continue;
+                    if (!(ok = mbar_wait(&p_full[t], j & 1, abort_flag, err, kErrWaitProb))) break;
+                    tc_fence_after();
+                    issue_pv(t, j);  // reads P_t(j) from TMEM: must precede S_t(j+1)
+                    if (j + 1 < nkv[t]) {
+                        if (!k_ready && !(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
+                        k_ready = true;
+                        tc_fence_after();
+                        issue_s(t, j + 1);  // overwrites S_t / P_t
+                    }
                 }
-                umma_commit(&v_empty[st]);
-                umma_commit(o_full);
+                if (!ok) break;
+                umma_commit(&v_empty[j & 1]);
+                if (more) umma_commit(&k_empty[(j + 1) & 1]);
             }
             umma_commit(mma_done);
             mbar_wait_drain(mma_done, 0, err);
         }
-    } else if (warp >= kFirstSoftWarp) {
-        // ----------------------------------------------------- softmax warps
-        const int sw = warp - kFirstSoftWarp;  // 0..7
-        const int quarter = warp & 3;          // TMEM lane quarter
-        const int half = sw >> 2;              // column half
-        const int row = quarter * 32 + lane;   // query row within the tile
-        const int q = q0 + row;
+    } else {
+        // ----------------------------------------------------- softmax (warps 2-5: tile A, 6-9: tile B)
+        const int t = (warp - 2) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int q = qt[t] * kBQ + row;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-        TIn *pbuf = reinterpret_cast<TIn *>(smem + L::kP + half * L::kChunk);
-
-        // exchange with the partner thread (same row, other half); returns the
-        // partner's value; `ok` becomes the pair-uniform conjunction of votes.
-        int xslot = 0;
-        auto exchange = [&](float v, bool &ok) -> float {
-            const int vote = __all_sync(0xffffffffu, ok) ? 1 : 0;
-            const int base = xslot * 256;
-            xch_v[base + half * 128 + row] = v;
-            xch_ok[base + half * 128 + row] = vote;
-            named_bar_sync(1 + quarter, 64);
-            const float other = xch_v[base + (half ^ 1) * 128 + row];
-            const int other_ok = xch_ok[base + (half ^ 1) * 128 + row];
-            ok = vote && other_ok;
-            xslot = (xslot + 1) & 3;
-            return other;
-        };
-
-        float m_run = -INFINITY, l_run = 0.0f;
+        const uint32_t ts = tmem_s[t] + lane_off, to = tmem_o[t] + lane_off;
+        const float c = args.scale_log2;
+        float m_used = -INFINITY, l_run = 0.0f;
         bool ok = true;
         int j = 0;
-        for (; j < n_kv; ++j) {
-            const int st = j & 1;
-            // ---- scores S_j (this thread's 64 columns of its row)
-            ok = mbar_wait(&s_full[st], (j >> 1) & 1, abort_flag, err, kErrWaitScore);
-            ok = __all_sync(0xffffffffu, ok);
-            float s[64];
-            float pmax = -INFINITY;
-            if (ok) {
-                tc_fence_after();
-                tmem_ld32f(tmem_s[st] + lane_off + half * 64, s);
-                tmem_ld32f(tmem_s[st] + lane_off + half * 64 + 32, s + 32);
-                tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(&s_empty[st]);
-                const int k0 = j * kBK + half * 64;
-                const bool need_mask = (args.causal && j == qt) || (j * kBK + kBK > args.seq);
-#pragma unroll
-                for (int i = 0; i < 64; ++i) s[i] *= args.scale_log2;
-                if (need_mask) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        const int key = k0 + i;
-                        if (key >= args.seq || (args.causal && key > q)) s[i] = -INFINITY;
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 64; ++i) pmax = fmaxf(pmax, s[i]);
-            }
-            const float other_max = exchange(pmax, ok);
+        for (; j < nkv[t]; ++j) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag, err, kErrWaitScore));
             if (!ok) break;
-            const float m_new = fmaxf(m_run, fmaxf(pmax, other_max));
-            const float alpha = fast_exp2(m_run - m_new);
-            m_run = m_new;
-            float psum = 0.0f;
+            tc_fence_after();
+            const bool need_mask = (args.causal && j == qt[t]) || (j * kBK + kBK > args.seq);
+            const int k0 = j * kBK;
+            // the whole row of S_t(j) in one round trip (one wait for four loads)
+            float sv[128];
+            tmem_ld32f(ts, sv);
+            tmem_ld32f(ts + 32, sv + 32);
+            tmem_ld32f(ts + 64, sv + 64);
+            tmem_ld32f(ts + 96, sv + 96);
+            tmem_wait_ld();
+            if (need_mask) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                s[i] = fast_exp2(s[i] - m_new);
-                psum += s[i];
-            }
-            l_run = l_run * alpha + psum;
-            // ---- P_{j-1} V_{j-1} must be done before P and O are touched
-            if (j > 0) {
-                ok = mbar_wait(o_full, (j - 1) & 1, abort_flag, err, kErrWaitPv);
-                (void)exchange(0.0f, ok);
-                if (!ok) break;
-            }
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                uint4 u;
-                if constexpr (kFmt == 1) {
-                    u.x = pack_bf16(s[8 * g + 0], s[8 * g + 1]); u.y = pack_bf16(s[8 * g + 2], s[8 * g + 3]);
-                    u.z = pack_bf16(s[8 * g + 4], s[8 * g + 5]); u.w = pack_bf16(s[8 * g + 6], s[8 * g + 7]);
-                } else {
-                    u.x = pack_f16(s[8 * g + 0], s[8 * g + 1]); u.y = pack_f16(s[8 * g + 2], s[8 * g + 3]);
-                    u.z = pack_f16(s[8 * g + 4], s[8 * g + 5]); u.w = pack_f16(s[8 * g + 6], s[8 * g + 7]);
+                for (int i = 0; i < 128; ++i) {
+                    const int key = k0 + i;
+                    if (key >= args.seq || (args.causal && key > q)) sv[i] = -INFINITY;
                 }
-                *reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(pbuf) + row * 128 + ((g ^ (row & 7)) << 4)) = u;
             }
-            fence_proxy_async();
-            // ---- rescale the running output O (in TMEM) to the new maxima; skipped
-            // when no row of this warp changed its maximum (alpha == 1 exactly)
+            float mx[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+#pragma unroll
+            for (int i = 8; i < 128; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
+            const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            const float m_tile = mraw * c;
+            // lazy rescale: keep the old maximum unless it grew by more than 2^8
+            float m_new = m_used, alpha = 1.0f;
+            if (j == 0) m_new = m_tile;
+            else if (m_tile > m_used + kRescaleThreshold) {
+                m_new = m_tile;
+                alpha = fast_exp2(m_used - m_new);
+            }
+            m_used = m_new;
+            // P = exp2(S*c - m) as 16-bit pairs over S's first 64 columns; masked
+            // scores are -inf, so exp2 gives exact zeros.
+            const float neg_m = -m_used;
+            float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
+                    const float p0 = fast_exp2(fmaf(sv[ch * 16 + i], c, neg_m));
+                    const float p1 = fast_exp2(fmaf(sv[ch * 16 + i + 1], c, neg_m));
+                    ps[(i >> 1) & 3] += p0 + p1;
+                    pk[i / 2] = kFmt == 1 ? pack_bf16(p0, p1) : pack_f16(p0, p1);
+                }
+                tmem_st8(ts + ch * 8, pk);
+            }
+            const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+            // O (in TMEM) to the new maxima, after P so the scores' registers are free
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-                tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < kHalfCols; c += 32) {
-                    float r[32];
-                    const uint32_t ta = tmem_o + lane_off + half * kHalfCols + c;
-                    tmem_ld32f(ta, r);
+                for (int oc = 0; oc < D; oc += 32) {
+                    float ov[32];
+                    tmem_ld32f(to + oc, ov);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] *= alpha;
-                    tmem_st32f(ta, r);
+                    for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                    tmem_st32f(to + oc, ov);
                 }
-                tmem_wait_st();
             }
+            l_run = l_run * alpha + psum;
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[t]);
         }
-        if (ok && j == n_kv) {
-            ok = mbar_wait(o_full, (n_kv - 1) & 1, abort_flag, err, kErrWaitPv);
-            ok = __all_sync(0xffffffffu, ok);
-            const float other_l = exchange(l_run, ok);
+        if (ok && nkv[t] > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], (nkv[t] - 1) & 1, abort_flag, err, kErrWaitPv));
             if (ok) {
                 tc_fence_after();
-                const float inv = 1.0f / (l_run + other_l);
-                TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * D + half * kHalfCols;
+                const float inv = 1.0f / l_run;
+                TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * D;
 #pragma unroll 1
-                for (int c = 0; c < kHalfCols; c += 32) {
+                for (int oc = 0; oc < D; oc += 32) {
                     float r[32];
-                    tmem_ld32f(tmem_o + lane_off + half * kHalfCols + c, r);
+                    tmem_ld32f(to + oc, r);
                     tmem_wait_ld();
                     if (q < args.seq) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 8) {
                             if constexpr (std::is_same<TOut, float>::value) {
-                                *reinterpret_cast<float4 *>(o + c + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
-                                *reinterpret_cast<float4 *>(o + c + e + 4) =
+                                *reinterpret_cast<float4 *>(o + oc + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
+                                *reinterpret_cast<float4 *>(o + oc + e + 4) =
                                     make_float4(r[e + 4] * inv, r[e + 5] * inv, r[e + 6] * inv, r[e + 7] * inv);
                             } else {
                                 uint4 u;
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     u.x = pack_f16(r[e] * inv, r[e + 1] * inv); u.y = pack_f16(r[e + 2] * inv, r[e + 3] * inv);
                                     u.z = pack_f16(r[e + 4] * inv, r[e + 5] * inv); u.w = pack_f16(r[e + 6] * inv, r[e + 7] * inv);
                                 }
-                                *reinterpret_cast<uint4 *>(o + c + e) = u;
+                                *reinterpret_cast<uint4 *>(o + oc + e) = u;
                             }
                         }
                     }
@@ -381,14 +384,15 @@ LaunchFn attn_launch(Context *ctx, const Spec &s) {
     const CUtensorMapDataType dt = std::is_same<TIn, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     AttnArgs base{};
     base.seq = (int)s.seq;
-    base.heads_total = (int)(s.batch * s.heads);
+    const int heads_total = (int)(s.batch * s.heads);
     base.nq_tiles = (int)((s.seq + kBQ - 1) / kBQ);
+    base.npairs = (base.nq_tiles + 1) / 2;
     base.nkv_tiles = (int)((s.seq + kBK - 1) / kBK);
     base.causal = s.causal ? 1 : 0;
     base.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
     base.err = ctx->err_dev;
-    const dim3 grid(base.heads_total, base.nq_tiles);
-    const uint64_t bh = base.heads_total, seq = s.seq;
+    const dim3 grid(heads_total, base.npairs);
+    const uint64_t bh = heads_total, seq = s.seq;
     return [=](cudaStream_t st, void **b) {
         CUtensorMap mq, mk, mv;
         if (!make_map3(&mq, dt, b[0], bh, seq, D) || !make_map3(&mk, dt, b[1], bh, seq, D) || !make_map3(&mv, dt, b[2], bh, seq, D))
@@ -405,7 +409,7 @@ LaunchFn attn_launch(Context *ctx, const Spec &s) {
 LaunchFn make_attention_tc(Context *ctx, const Spec &s, std::string &impl) {
     if (s.op != Op::AttentionOnline) throw IrError("only attention_online has a tensor-core path");
     if (!encoder()) throw IrError("cuTensorMapEncodeTiled unavailable");
-    impl = std::string("attention_tcgen05_fa_q128_kv128_d") + std::to_string(s.dim) + "_" + dtype_name(s.dtype) + "_out_" +
+    impl = std::string("attention_tcgen05_fa_2xq128_kv128_d") + std::to_string(s.dim) + "_" + dtype_name(s.dtype) + "_out_" +
            dtype_name(s.out_dtype) + (s.causal ? "_causal" : "");
     const bool f32out = s.out_dtype == DType::F32;
     if (s.dtype == DType::BF16) {

@@ -177,9 +177,9 @@ template <> struct Vec<__nv_bfloat16> {
 // each thread holds NV vectors. Requires cols % Vec::N == 0 and cols <= NV*N*blockDim.
 enum class RowOp { RmsNorm, Softmax, RmsInv };
 
-template <typename T, int NV, RowOp OP>
-__global__ void __launch_bounds__(kThreads) row_kernel(const T *__restrict__ x, const T *__restrict__ w, void *__restrict__ out_,
-                                                       uint32_t rows, uint32_t cols, float eps) {
+template <typename T, int NV, RowOp OP, int THREADS>
+__global__ void __launch_bounds__(THREADS) row_kernel(const T *__restrict__ x, const T *__restrict__ w, void *__restrict__ out_,
+                                                      uint32_t rows, uint32_t cols, float eps) {
     __shared__ float scratch[32];
     constexpr int N = Vec<T>::N;
     const uint32_t nvec = cols / N;
@@ -188,21 +188,22 @@ __global__ void __launch_bounds__(kThreads) row_kernel(const T *__restrict__ x, 
         float v[NV][N];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            const uint32_t c = threadIdx.x + j * blockDim.x;
+            const uint32_t c = threadIdx.x + j * THREADS;
             if (c < nvec) Vec<T>::load(xr + (uint64_t)c * N, v[j]);
         }
+
         if constexpr (OP == RowOp::Softmax) {
             float m = -INFINITY;
 #pragma unroll
             for (int j = 0; j < NV; ++j)
-                if (threadIdx.x + j * blockDim.x < nvec)
+                if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
                     for (int e = 0; e < N; ++e) m = fmaxf(m, v[j][e]);
             m = block_reduce<true>(m, scratch);
             float s = 0.0f;
 #pragma unroll
             for (int j = 0; j < NV; ++j)
-                if (threadIdx.x + j * blockDim.x < nvec)
+                if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
                     for (int e = 0; e < N; ++e) { v[j][e] = expf(v[j][e] - m); s += v[j][e]; }
             s = block_reduce<false>(s, scratch);
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(kThreads) row_kernel(const T *__restrict__ x, 
             T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
-                const uint32_t c = threadIdx.x + j * blockDim.x;
+                const uint32_t c = threadIdx.x + j * THREADS;
                 if (c < nvec) {
 #pragma unroll
                     for (int e = 0; e < N; ++e) v[j][e] *= inv;
@@ -221,7 +222,7 @@ __global__ void __launch_bounds__(kThreads) row_kernel(const T *__restrict__ x, 
             float ss = 0.0f;
 #pragma unroll
             for (int j = 0; j < NV; ++j)
-                if (threadIdx.x + j * blockDim.x < nvec)
+                if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
                     for (int e = 0; e < N; ++e) ss = fmaf(v[j][e], v[j][e], ss);
             ss = block_reduce<false>(ss, scratch);
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(kThreads) row_kernel(const T *__restrict__ x, 
                 T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
 #pragma unroll
                 for (int j = 0; j < NV; ++j) {
-                    const uint32_t c = threadIdx.x + j * blockDim.x;
+                    const uint32_t c = threadIdx.x + j * THREADS;
                     if (c < nvec) {
                         float wv[N];
                         Vec<T>::load_keep(w + (uint64_t)c * N, wv);
@@ -286,21 +287,29 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
     const float eps = s.epsilon;
     const int grid = grid_for(ctx, rows, 1, 16);
     const bool vec = cols % N == 0;
-    const uint32_t per_thread = (cols / N + kThreads - 1) / kThreads;  // vectors per thread
+    // Rows of up to 8 vectors per thread at 128 threads run 128-thread blocks (up
+    // to 16 rows in flight per SM); wider rows use 256 threads.
+    const uint32_t nv = cols / N;
+    const int threads = (vec && nv <= 128 * 8) ? 128 : kThreads;
+    const uint32_t per_thread = (nv + threads - 1) / threads;  // vectors per thread
     using KFn = void (*)(const T *, const T *, void *, uint32_t, uint32_t, float);
     KFn fn = nullptr;
-    if (vec && per_thread <= 1) fn = row_kernel<T, 1, OP>;
-    else if (vec && per_thread <= 2) fn = row_kernel<T, 2, OP>;
-    else if (vec && per_thread <= 4) fn = row_kernel<T, 4, OP>;
-    else if (vec && per_thread <= 8) fn = row_kernel<T, 8, OP>;
-    else if (vec && per_thread <= 16) fn = row_kernel<T, 16, OP>;
+    if (threads == 128) {
+        if (per_thread <= 1) fn = row_kernel<T, 1, OP, 128>;
+        else if (per_thread <= 2) fn = row_kernel<T, 2, OP, 128>;
+        else if (per_thread <= 4) fn = row_kernel<T, 4, OP, 128>;
+        else fn = row_kernel<T, 8, OP, 128>;
+    } else if (vec && per_thread <= 8) fn = row_kernel<T, 8, OP, 256>;
+    else if (vec && per_thread <= 16) fn = row_kernel<T, 16, OP, 256>;
     else fn = row_kernel_general<T, OP>;
-    impl = std::string(fn == (KFn)row_kernel_general<T, OP> ? "row_general_" : "row_register_") + dtype_name(s.dtype);
+    const int grid2 = threads == 128 ? grid_for(ctx, rows, 1, 32) : grid;
+    impl = std::string(fn == (KFn)row_kernel_general<T, OP> ? "row_general_" : "row_register_") + dtype_name(s.dtype) + "_t" +
+           std::to_string(threads);
     return [=](cudaStream_t st, void **b) {
         const T *x = static_cast<const T *>(b[0]);
         const T *w = OP == RowOp::RmsNorm ? static_cast<const T *>(b[1]) : nullptr;
         void *out = OP == RowOp::RmsNorm ? b[2] : b[1];
-        fn<<<grid, kThreads, 0, st>>>(x, w, out, rows, cols, eps);
+        fn<<<grid2, threads, 0, st>>>(x, w, out, rows, cols, eps);
         return cudaGetLastError();
     };
 }
