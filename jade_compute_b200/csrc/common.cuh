@@ -235,21 +235,6 @@ template <> __device__ __forceinline__ float from_f32<float>(float v) { return v
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
-// 2^x on the FMA/ALU pipes (no MUFU): x = n + f with n = round(x), f in [-0.5, 0.5];
-// 2^f from a degree-3 polynomial fitted here by relative-error least squares
-// (max relative error 7.5e-5, below the 2^-9 rounding of a BF16/FP16 result);
-// 2^n added to the exponent bits. x is clamped to [-125, 126], so results stay
-// normal; callers that need an exact 0 for -inf inputs apply their mask after.
-__device__ __forceinline__ float exp2_poly3(float x) {
-    x = fminf(fmaxf(x, -125.0f), 126.0f);
-    const float shifter = 12582912.0f;  // 1.5 * 2^23: rounds x to an integer in the low mantissa bits
-    const float t = x + shifter;
-    const float f = x - (t - shifter);
-    float p = fmaf(fmaf(fmaf(0.05517165f, f, 0.24261116f), f, 0.69326099f), f, 0.99992807f);
-    const int n = __float_as_int(t) - 0x4B400000;
-    return __int_as_float(__float_as_int(p) + (n << 23));
-}
-
 // Stable logistic function in the reference's branch form (src/runtime/ir.rs:487).
 __device__ __forceinline__ float stable_sigmoid(float v) {
     const float e = expf(-fabsf(v));
