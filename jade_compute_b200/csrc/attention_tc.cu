@@ -26,6 +26,7 @@
 // Every wait is bounded; an abort makes each warp leave at a warp-uniform point.
 #include <cuda.h>
 
+#include <climits>
 #include <mutex>
 #include <type_traits>
 
@@ -251,12 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32f(ts + 64, sv + 64);
             tmem_ld32f(ts + 96, sv + 96);
             tmem_wait_ld();
-            if (need_mask) {
+            if (need_mask) {  // keys k0 + i with i > lim are invisible to this row
+                const int lim = min(args.seq - 1, args.causal ? q : INT_MAX) - k0;
 #pragma unroll
-                for (int i = 0; i < 128; ++i) {
-                    const int key = k0 + i;
-                    if (key >= args.seq || (args.causal && key > q)) sv[i] = -INFINITY;
-                }
+                for (int i = 0; i < 128; ++i) sv[i] = i <= lim ? sv[i] : -INFINITY;
             }
             float mx[8];
 #pragma unroll
