@@ -1,0 +1,679 @@
+// Forward attention for head dim 128 on tcgen05 pairs of SMs (cta_group::2).
+//
+// Semantics are those of attention_tc.cu (the reference's online attention,
+// src/runtime/metal_attention.rs:44-137, oracle src/runtime/metal_lab.rs:33-73,
+// extended to [batch, heads, seq, dim] and a causal mask): O = softmax(Q K^T /
+// sqrt(D)) V with FP32 softmax statistics, P rounded to the input type for P.V
+// and O accumulated in FP32 in TMEM.
+//
+// A cluster of two CTAs (one per SM) owns 256 query rows of one (batch, head):
+// CTA r holds rows [128 r, 128 r + 128) and each tensor-core instruction of the
+// pair is an M=256 MMA issued by CTA 0. The B operand of every MMA is split by
+// N between the two CTAs' shared memory, so each SM streams half of every K
+// tile (64 keys x 128 dims) and half of every V tile (128 keys x 64 dims):
+// the K/V bytes per SM per key step are those of a 256-row tile on one SM.
+//
+// TMEM per CTA: S0 | S1 | S2 | O (128 columns each). S is triple-buffered: S(j+3)
+// is issued right behind P(j).V(j) into the buffer P(j) came from (same issuing
+// thread, so in order), and S(j+1), S(j+2) are already computed when the softmax
+// of S(j) ends, so the tensor core never sits on the softmax's critical path.
+//
+//   warp 0     TMA producer (both CTAs): own Q rows once; own K/V halves into
+//              four-stage rings; completion is counted on CTA 0's barriers.
+//   warp 1     CTA 0: MMA issuer  S(0) S(1) S(2) | P(j).V(j) S(j+3) ...
+//              CTA 1: relays its softmax warps' "P(j) written" to CTA 0
+//   warps 2-9  softmax: warps w and w+4 share TMEM lane quarter w%4 and split
+//              each row's 128 keys in halves; they exchange half-row maxima per
+//              step through shared memory so both use the same running maximum.
+//              P(j) (16-bit pairs) is written over the half's own S columns.
+// O is rescaled in place only when a row maximum grows by more than 2^8; the
+// rescale first waits for P(j-1).V(j-1). A small fixed share of the exponentials
+// of unmasked tiles is evaluated with a cubic polynomial on the FMA pipe instead
+// of the MUFU unit, which is the softmax bottleneck.
+// Every wait is bounded (the error word records where it gave up); every thread
+// of both CTAs reaches the final cluster barrier, after which TMEM is released.
+#include <cuda.h>
+
+#include <climits>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "internal.hpp"
+
+namespace jade {
+namespace {
+
+constexpr int kRows = 128;     // query rows per CTA
+constexpr int kKeys = 128;     // keys per step
+constexpr int kDim = 128;      // head dim
+constexpr int kStages = 4;     // K and V ring depth
+// two softmax warps per TMEM lane quarter: one takes the even key steps, the
+// other the odd ones, each thread a whole row (128 scores) of its steps
+constexpr int kCols = kKeys;
+constexpr int kThreads = 10 * 32;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// exponentials per 16-element group evaluated by the polynomial (unmasked tiles)
+constexpr int kPolyPairs = 1;
+
+struct Layout {
+    static constexpr uint32_t kQ = 0;                 // 2 chunks x 16 KB (128 rows x 64 dims, SW128)
+    static constexpr uint32_t kKStage = 16384;        // 2 chunks x 8 KB (64 keys x 64 dims)
+    static constexpr uint32_t kVStage = 16384;        // 128 keys x 64 dims
+    static constexpr uint32_t kK = kQ + 32768;
+    static constexpr uint32_t kV = kK + kStages * kKStage;
+    // never written: keeps any operand window that a descriptor could describe
+    // past the last V stage inside the allocation
+    static constexpr uint32_t kGuard = kV + kStages * kVStage;
+    static constexpr uint32_t kBar = kGuard + 32768;
+    static constexpr uint32_t kRed = kBar + 512;      // float [2][128] running maxima, [2][128] row sums
+    static constexpr uint32_t kSmem = kRed + 2 * 2 * 128 * 4 + 1024;
+};
+
+struct Args {
+    void *out;
+    int seq, nq_tiles, npairs, nkv_tiles, causal;
+    float scale_log2;
+    int *err;
+};
+
+// ---------------------------------------------------------------- cluster helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Arrival on an mbarrier of either CTA. P reaches the tensor core through TMEM,
+// ordered by tcgen05.wait::st and tcgen05.fence before this arrive, so the arrive
+// needs no cluster-scope release (which costs about a microsecond per step).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded polling wait (no suspension: the phases waited on here complete within
+// a few hundred cycles, and a suspended waiter can resume much later than that).
+__device__ __forceinline__ bool mbar_spin(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err, int code) {
+    if (mbar_test_wait(bar, parity)) return true;  // usual case: no timer read
+    const uint64_t t0 = globaltimer();
+#pragma unroll 1
+    while (true) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > JADE_WAIT_LIMIT_NS) {
+            if (err) atomicCAS(err, 0, code);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+// TMA tile load into this CTA's shared memory whose completion is counted on an
+// mbarrier of this CTA or of its peer (CTA 0 counts both CTAs' bytes).
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar_cluster_addr, int32_t c0, int32_t c1,
+                                                 int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// The issuing helpers below are executed by a whole converged warp and issue
+// from one elected lane: issuing from a single divergent thread starves the
+// tensor core when the SM sub-partition is shared with busy softmax warps.
+// D[tmem] (+)= A[smem] * B[smem], M=256 over the CTA pair.
+__device__ __forceinline__ void umma_pair_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem], M=256 over the CTA pair.
+__device__ __forceinline__ void umma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// One arrival on the mbarrier at `bar_cluster_addr` (either CTA) once every
+// tcgen05 operation issued so far by the elected thread has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar_cluster_addr)
+        : "memory");
+}
+
+// ---------------------------------------------------------------- softmax arithmetic
+__device__ __forceinline__ uint64_t pack2f(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2f(uint64_t v, float &a, float &b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float mufu_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+template <uint32_t kFmt>
+__device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+    return kFmt == 1 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+}
+// 2^x for two finite x on the FMA pipe: x = n + f with n = round(x), |f| <= 1/2,
+// 2^f by a cubic (relative-error least-squares fit on [-1/2, 1/2], max relative
+// error 7.5e-5, below the 16-bit rounding of P), 2^n added to the exponent field.
+// x is clamped to -125 so the exponent stays in the normal range (results below
+// 2^-125 are returned as about 2^-125 instead of smaller values).
+__device__ __forceinline__ uint64_t poly_exp2_pair(uint64_t x) {
+    float x0, x1;
+    unpack2f(x, x0, x1);
+    const uint64_t xc = pack2f(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+    const uint64_t shifter = pack2f(12582912.0f, 12582912.0f);  // 1.5 * 2^23: adding it rounds to an integer
+    const uint64_t t = add2(xc, shifter);
+    const uint64_t f = sub2(xc, sub2(t, shifter));
+    uint64_t p = fma2(pack2f(0.055171635f, 0.055171635f), f, pack2f(0.24261113f, 0.24261113f));
+    p = fma2(p, f, pack2f(0.69326097f, 0.69326097f));
+    p = fma2(p, f, pack2f(0.99992806f, 0.99992806f));
+    float t0, t1, p0, p1;
+    unpack2f(t, t0, t1);
+    unpack2f(p, p0, p1);
+    // the low mantissa bits of t hold n (two's complement); shifting by 23 moves n
+    // into the exponent field and drops the shifter's own bits
+    const float r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    const float r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+    return pack2f(r0, r1);
+}
+
+// Makes the compiler treat v as written here: uses of registers filled by an
+// asynchronous tcgen05.ld stay behind the tcgen05.wait::ld that precedes this.
+template <int N>
+__device__ __forceinline__ void reg_fence(float (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
+}
+// P = exp2(s * c - m) for a row of scores, written as 16-bit pairs to TMEM
+// columns [ts, ts + kCols/2) eight at a time; returns the row sum.
+// kPoly: evaluate kPolyPairs of every 8 pairs with the FMA-pipe polynomial.
+template <uint32_t kFmt, bool kPoly>
+__device__ __forceinline__ float store_p(const float (&sv)[kCols], float c, float m, uint32_t ts) {
+    const uint64_t c2 = pack2f(c, c), nm2 = pack2f(-m, -m);
+    uint64_t acc[2] = {pack2f(0.0f, 0.0f), pack2f(0.0f, 0.0f)};
+#pragma unroll
+    for (int g = 0; g < kCols / 16; ++g) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint64_t xv = fma2(pack2f(sv[16 * g + 2 * i], sv[16 * g + 2 * i + 1]), c2, nm2);
+            uint64_t p;
+            if (kPoly && i < kPolyPairs) {
+                p = poly_exp2_pair(xv);
+            } else {
+                float x0, x1;
+                unpack2f(xv, x0, x1);
+                p = pack2f(mufu_exp2(x0), mufu_exp2(x1));
+            }
+            acc[i & 1] = add2(acc[i & 1], p);
+            float p0, p1;
+            unpack2f(p, p0, p1);
+            pk[i] = pack16<kFmt>(p0, p1);
+        }
+        tmem_st8(ts + g * 8, pk);
+    }
+    float a0, a1, b0, b1;
+    unpack2f(acc[0], a0, a1);
+    unpack2f(acc[1], b0, b1);
+    return (a0 + a1) + (b0 + b1);
+}
+
+template <typename TIn, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const Args args) {
+    using L = Layout;
+    constexpr uint32_t kFmt = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
+    constexpr uint32_t kIdescS = idesc_f32acc(kFmt, kFmt, false, false, 2 * kRows, kKeys);
+    constexpr uint32_t kIdescO = idesc_f32acc(kFmt, kFmt, false, true, 2 * kRows, kDim);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBar);
+    uint64_t *q_full = bars + 0;
+    uint64_t *k_full = bars + 1, *k_empty = bars + 5, *v_full = bars + 9, *v_empty = bars + 13;  // [stage]
+    uint64_t *s_full = bars + 17, *p_full = bars + 20;                                         // [S buffer]
+    // P(j).V(j) done, for the O rescale: S(j+3) in general (issued right behind it);
+    // o_tail[0], o_tail[1] for the last two steps, o_last for the final one
+    uint64_t *o_tail = bars + 23, *o_last = bars + 25;
+    uint64_t *pub = bars + 26;  // [lane quarter][step parity]: running maximum after a step published
+    uint64_t *fin = bars + 34;  // [lane quarter]: both warps' final maxima and sums posted
+    uint64_t *mma_done = bars + 38;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 39);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *red = reinterpret_cast<float *>(smem + L::kRed);  // [2][2][128]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int bh = blockIdx.y;
+    const int pair = args.npairs - 1 - (int)blockIdx.z;  // heaviest causal pairs first
+    const int q0 = (2 * pair + (int)rank) * kRows;
+    const int nsteps = args.causal ? min(2 * pair + 2, args.nkv_tiles) : args.nkv_tiles;
+    int *err = args.err;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1);
+        }
+        for (int b = 0; b < 3; ++b) {
+            mbar_init(&s_full[b], 1);
+            // CTA 0: its softmax warps + one forwarded arrival for CTA 1's softmax warps
+            mbar_init(&p_full[b], 4 + (leader ? 1 : 0));
+        }
+        mbar_init(&o_tail[0], 1);
+        mbar_init(&o_tail[1], 1);
+        mbar_init(o_last, 1);
+        for (int q = 0; q < 8; ++q) mbar_init(&pub[q], 32);
+        for (int q = 0; q < 4; ++q) mbar_init(&fin[q], 64);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers and TMEM of both CTAs exist before any cross-CTA use
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem_o = tmem + 384;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ------------------------------------- TMA producer (both CTAs)
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            const uint32_t q_full_lead = map_rank(smem_u32(q_full), 0);
+            if (leader) mbar_arrive_expect_tx(q_full, 2 * 32768);
+            for (int c = 0; c < 2; ++c) tma_load_3d_pair(smem + L::kQ + c * 16384, &tmQ, q_full_lead, c * 64, q0, bh);
+            int issued = 0;
+            for (int j = 0; j < nsteps && !*abort_flag; ++j) {
+                const int st = j % kStages;
+                const uint32_t ph = (j / kStages) & 1;
+                if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
+                if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * L::kKStage);
+                const uint32_t kf = map_rank(smem_u32(&k_full[st]), 0);
+                for (int c = 0; c < 2; ++c)
+                    tma_load_3d_pair(smem + L::kK + st * L::kKStage + c * 8192, &tmK, kf, c * 64, j * kKeys + (int)rank * 64, bh);
+                if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
+                if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * L::kVStage);
+                tma_load_3d_pair(smem + L::kV + st * L::kVStage, &tmV, map_rank(smem_u32(&v_full[st]), 0), (int)rank * 64, j * kKeys, bh);
+                issued = j + 1;
+            }
+            if (*abort_flag && leader) {  // CTA 0 counts both CTAs' copies: wait for those still in flight
+                mbar_wait_drain(q_full, 0, err);
+                for (int j = max(0, issued - kStages); j < issued; ++j) {
+                    mbar_wait_drain(&k_full[j % kStages], (j / kStages) & 1, err);
+                    mbar_wait_drain(&v_full[j % kStages], (j / kStages) & 1, err);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader) {  // ------------------------------- MMA issuer (CTA 0, whole warp, one elected lane issues)
+            const uint32_t sq = smem_u32(smem + L::kQ);
+            auto commit_both = [&](uint64_t *bar) {
+                umma_commit_pair(smem_u32(bar));
+                umma_commit_pair(map_rank(smem_u32(bar), 1));
+            };
+            // polling waits: a suspended waiter resumes a few hundred cycles after
+            // the phase completes, and this warp waits three times per key step
+            auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
+                return __all_sync(0xffffffffu, mbar_spin(bar, parity, abort_flag, err, code));
+            };
+            bool ok = wait(q_full, 0, kErrWaitTmaFull);
+            auto issue_s = [&](int j, bool wait_k) {  // S(j) = Q K_j^T into buffer j % 3
+                const int st = j % kStages;
+                if (wait_k && !wait(&k_full[st], (j / kStages) & 1, kErrWaitTmaFull)) return false;
+                tc_fence_after();
+                const uint32_t sk = smem_u32(smem + L::kK + st * L::kKStage);
+#pragma unroll
+                for (int k = 0; k < kDim / 16; ++k)
+                    umma_pair_ss(tmem + (j % 3) * 128, sdesc_sw128(sq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                                 sdesc_sw128(sk + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024), kIdescS, k != 0);
+                commit_both(&s_full[j % 3]);
+                commit_both(&k_empty[st]);
+                return true;
+            };
+            for (int j = 0; ok && j < 3 && j < nsteps; ++j) ok = issue_s(j, true);
+            for (int j = 0; ok && j < nsteps; ++j) {
+                const int st = j % kStages, st3 = (j + 3) % kStages;
+                const bool more = j + 3 < nsteps;
+                // this step's inputs (P(j), V(j), K(j+3)) are tested together so the
+                // barrier latencies overlap; the bounded waits run only if one is missing
+                const bool rp = mbar_test_wait(&p_full[j % 3], (j / 3) & 1);
+                const bool rv = mbar_test_wait(&v_full[st], (j / kStages) & 1);
+                const bool rk = !more || mbar_test_wait(&k_full[st3], ((j + 3) / kStages) & 1);
+                if (!__all_sync(0xffffffffu, rp && rv && rk)) {
+                    if (!(ok = wait(&p_full[j % 3], (j / 3) & 1, kErrWaitProb))) break;
+                    if (!(ok = wait(&v_full[st], (j / kStages) & 1, kErrWaitTmaFull))) break;
+                    if (more && !(ok = wait(&k_full[st3], ((j + 3) / kStages) & 1, kErrWaitTmaFull))) break;
+                }
+                tc_fence_after();
+                const uint32_t sv = smem_u32(smem + L::kV + st * L::kVStage);
+                const uint32_t sp = tmem + (j % 3) * 128;
+#pragma unroll
+                for (int k = 0; k < kKeys / 16; ++k)  // keys 16k..16k+15: P columns 8k..8k+7
+                    umma_pair_ts(tmem_o, sp + k * 8, sdesc_sw128(sv + k * 2048, 16384, 1024), kIdescO,
+                                 (j | k) != 0);
+                commit_both(&v_empty[st]);
+                if (j == nsteps - 3) commit_both(&o_tail[0]);
+                if (j == nsteps - 2) commit_both(&o_tail[1]);
+                if (j == nsteps - 1) commit_both(o_last);
+                if (more) issue_s(j + 3, false);  // reuses P(j)'s buffer: after P(j).V(j) in issue order
+            }
+            umma_commit_pair(smem_u32(mma_done));
+            mbar_wait_drain(mma_done, 0, err);
+        } else if (lane == 0) {  // --------------------------- P forwarder (CTA 1)
+            // One remote arrival per step instead of one per softmax warp: an
+            // arrival on the peer's barrier stalls the arriving warp for hundreds
+            // of cycles, so the softmax warps arrive locally and this thread relays.
+            for (int j = 0; j < nsteps; ++j) {
+                if (!mbar_spin(&p_full[j % 3], (j / 3) & 1, abort_flag, err, kErrWaitProb)) break;
+                tc_fence_after();
+                tc_fence_before();
+                mbar_arrive_remote(map_rank(smem_u32(&p_full[j % 3]), 0));
+            }
+        }
+    } else {
+        // ----------------------------------------------------- softmax (warps 2-9, both CTAs)
+        // Warp pair (w, w + 4) shares lane quarter w % 4: warp parity p = (w - 2) / 4
+        // takes steps j = p, p + 2, ... with one thread per row. The running
+        // maximum m is passed along the steps through shared memory: step j's
+        // owner computes P(j) with the maximum it last saw, then reads step j-1's
+        // published maximum; if that moved, it redoes P(j) (and rescales its row
+        // sum). If the row maximum grows by more than 2^8 it raises m, redoes P(j)
+        // and rescales O after P(j-1).V(j-1) has landed. Consecutive steps of the
+        // two warps overlap, so one computes while the other waits.
+        const int quarter = warp & 3;
+        const int par = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int q = q0 + row;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        const float c = args.scale_log2;
+        float *tok = red;  // [2][128]: running maximum after the last step of each parity
+        float m_view = -INFINITY, l_own = 0.0f;  // l_own is in the scale of m_view
+        bool ok = true;
+        for (int j = par; ok && j < nsteps; j += 2) {
+            const int b = j % 3;
+            const uint32_t ts = tmem + b * 128 + lane_off;
+            ok = __all_sync(0xffffffffu, mbar_spin(&s_full[b], (j / 3) & 1, abort_flag, err, kErrWaitScore));
+            if (!ok) break;
+            tc_fence_after();
+            float sv[kCols];
+#pragma unroll
+            for (int cc = 0; cc < kCols; cc += 32) tmem_ld32f(ts + cc, sv + cc);
+            tmem_wait_ld();
+            reg_fence(sv);
+            const int k0 = j * kKeys;
+            const bool need_mask = (args.causal && k0 + kKeys - 1 > q0) || (k0 + kKeys > args.seq);
+            if (need_mask) {  // keys k0 + i with i > lim are invisible to this row
+                const int lim = min(args.seq - 1, args.causal ? q : INT_MAX) - k0;
+#pragma unroll
+                for (int i = 0; i < kCols; ++i) sv[i] = i <= lim ? sv[i] : -INFINITY;
+            }
+            float mx[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[e + 8], sv[e + 16]);
+#pragma unroll
+            for (int i = 24; i < kCols - 8; i += 16)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kCols - 8 + e]);
+            const float m_tile = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * c;
+            // the maximum published by step j-1 (its owner is the other warp of the pair)
+            auto read_prev = [&]() {
+                if (!__all_sync(0xffffffffu, mbar_spin(&pub[quarter * 2 + (par ^ 1)], ((j - 1) >> 1) & 1, abort_flag, err, kErrWaitScore)))
+                    return false;
+                const float m_prev = tok[(par ^ 1) * 128 + row];
+                if (m_prev != m_view) {  // the other warp raised m since this warp's last step
+                    l_own *= m_view == -INFINITY ? 0.0f : mufu_exp2(m_view - m_prev);
+                    m_view = m_prev;
+                }
+                return true;
+            };
+            float psum = 0.0f;
+            bool fresh = false;  // P(j) in TMEM was computed with the current m_view
+            if (j == 0) {
+                m_view = m_tile;
+            } else if (m_view == -INFINITY) {  // first step of the odd warp: nothing to speculate with
+                if (!(ok = read_prev())) break;
+            } else {
+                const float m_spec = m_view;
+                psum = need_mask ? store_p<kFmt, false>(sv, c, m_spec, ts) : store_p<kFmt, kFmt == 1>(sv, c, m_spec, ts);
+                if (!(ok = read_prev())) break;
+                fresh = __all_sync(0xffffffffu, m_view == m_spec);
+            }
+            float alpha = 1.0f;
+            if (j > 0 && __any_sync(0xffffffffu, m_tile > m_view + kRescaleThreshold)) {
+                if (m_tile > m_view + kRescaleThreshold) {
+                    alpha = mufu_exp2(m_view - m_tile);
+                    m_view = m_tile;
+                }
+                fresh = false;
+                // O (in TMEM) to the new maxima once P(j-1).V(j-1) has landed: S(j+2)
+                // was issued right behind it (its next phase needs P(j+2) from this
+                // warp, so the wait cannot alias); the last two steps have o_tail.
+                if (j + 2 < nsteps)
+                    ok = __all_sync(0xffffffffu, mbar_wait(&s_full[(j + 2) % 3], ((j + 2) / 3) & 1, abort_flag, err, kErrWaitPv));
+                else
+                    ok = __all_sync(0xffffffffu, mbar_wait(&o_tail[j + 2 - nsteps], 0, abort_flag, err, kErrWaitPv));
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int oc = 0; oc < kDim; oc += 32) {
+                    float ov[32];
+                    tmem_ld32f(tmem_o + lane_off + oc, ov);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                    tmem_st32f(tmem_o + lane_off + oc, ov);
+                }
+                l_own *= alpha;
+            }
+            if (!fresh) psum = store_p<kFmt, false>(sv, c, m_view, ts);
+            l_own += psum;
+            // publish the running maximum after step j for the owner of step j+1
+            tok[par * 128 + row] = m_view;
+            mbar_arrive(&pub[quarter * 2 + par]);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[b]);
+        }
+        if (ok && nsteps > 0) {
+            // row sum: both warps' sums brought to the final (largest) maximum;
+            // a warp's last publication equals its m_view, a warp without steps has -inf
+            float *lsum = red + 256;  // [2][128]
+            tok[par * 128 + row] = m_view;
+            lsum[par * 128 + row] = l_own;
+            mbar_arrive(&fin[quarter]);
+            ok = __all_sync(0xffffffffu, mbar_spin(&fin[quarter], 0, abort_flag, err, kErrWaitScore));
+            float l_row = 0.0f;
+            if (ok) {
+                const float m_other = tok[(par ^ 1) * 128 + row], l_other = lsum[(par ^ 1) * 128 + row];
+                const float m_final = fmaxf(m_view, m_other);
+                l_row = (l_own > 0.0f ? l_own * mufu_exp2(m_view - m_final) : 0.0f) +
+                        (l_other > 0.0f ? l_other * mufu_exp2(m_other - m_final) : 0.0f);
+            }
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_last, 0, abort_flag, err, kErrWaitPv));
+            if (ok) {
+                const float inv = 1.0f / l_row;
+                tc_fence_after();
+                // each warp of the pair writes half of the row's output columns
+                TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * kDim + par * 64;
+#pragma unroll 1
+                for (int oc = 0; oc < 64; oc += 32) {
+                    float r[32];
+                    tmem_ld32f(tmem_o + lane_off + par * 64 + oc, r);
+                    tmem_wait_ld();
+                    if (q < args.seq) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 8) {
+                            if constexpr (std::is_same<TOut, float>::value) {
+                                *reinterpret_cast<float4 *>(o + oc + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
+                                *reinterpret_cast<float4 *>(o + oc + e + 4) =
+                                    make_float4(r[e + 4] * inv, r[e + 5] * inv, r[e + 6] * inv, r[e + 7] * inv);
+                            } else {
+                                uint4 u;
+                                u.x = pack16<kFmt>(r[e] * inv, r[e + 1] * inv);
+                                u.y = pack16<kFmt>(r[e + 2] * inv, r[e + 3] * inv);
+                                u.z = pack16<kFmt>(r[e + 4] * inv, r[e + 5] * inv);
+                                u.w = pack16<kFmt>(r[e + 6] * inv, r[e + 7] * inv);
+                                *reinterpret_cast<uint4 *>(o + oc + e) = u;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // every thread of both CTAs: the pair's MMAs and TMEM reads are over
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *, const cuuint64_t *,
+                              const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encoder() {
+    static EncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] { fn = reinterpret_cast<EncodeFn>(driver_entry("cuTensorMapEncodeTiled")); });
+    return fn;
+}
+
+// [bh, seq, 128] tensor, box {64, rows, 1}, 128-byte swizzle.
+bool make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_t bh, uint64_t seq, uint32_t rows) {
+    EncodeFn enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {kDim, seq, bh};
+    const cuuint64_t strides[2] = {kDim * 2, seq * kDim * 2};
+    const cuuint32_t box[3] = {64, rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, dt, 3, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename TIn, typename TOut>
+LaunchFn pair_launch(Context *ctx, const Spec &s) {
+    auto kernel = attention_pair_kernel<TIn, TOut>;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Layout::kSmem) != cudaSuccess)
+        throw IrError("cannot reserve shared memory for the tcgen05 pair attention");
+    const CUtensorMapDataType dt = std::is_same<TIn, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    Args base{};
+    base.seq = (int)s.seq;
+    const int heads_total = (int)(s.batch * s.heads);
+    base.nq_tiles = (int)((s.seq + kRows - 1) / kRows);
+    base.npairs = (base.nq_tiles + 1) / 2;
+    base.nkv_tiles = (int)((s.seq + kKeys - 1) / kKeys);
+    base.causal = s.causal ? 1 : 0;
+    base.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)kDim));
+    base.err = ctx->err_dev;
+    if (heads_total > 65535 || base.npairs > 65535) throw IrError("attention grid too large for the pair kernel");
+    const dim3 grid(2, heads_total, base.npairs);
+    const uint64_t bh = heads_total, seq = s.seq;
+    return [=](cudaStream_t st, void **b) {
+        CUtensorMap mq, mk, mv;
+        if (!make_map(&mq, dt, b[0], bh, seq, 128) || !make_map(&mk, dt, b[1], bh, seq, 64) || !make_map(&mv, dt, b[2], bh, seq, 128))
+            return cudaErrorInvalidValue;
+        Args a = base;
+        a.out = b[3];
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Layout::kSmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, a);
+    };
+}
+
+}  // namespace
+
+// Head dim 128, BF16/FP16 inputs: the CTA-pair kernel above.
+LaunchFn make_attention_pair(Context *ctx, const Spec &s, std::string &impl) {
+    if (s.op != Op::AttentionOnline || s.dim != 128) throw IrError("the pair attention kernel covers attention_online with dim 128");
+    if (!encoder()) throw IrError("cuTensorMapEncodeTiled unavailable");
+    impl = std::string("attention_tcgen05_fa_pair_q256_kv128_d128_") + dtype_name(s.dtype) + "_out_" + dtype_name(s.out_dtype) +
+           (s.causal ? "_causal" : "");
+    const bool f32out = s.out_dtype == DType::F32;
+    if (s.dtype == DType::BF16)
+        return f32out ? pair_launch<__nv_bfloat16, float>(ctx, s) : pair_launch<__nv_bfloat16, __nv_bfloat16>(ctx, s);
+    return f32out ? pair_launch<__half, float>(ctx, s) : pair_launch<__half, __half>(ctx, s);
+}
+
+}  // namespace jade

@@ -63,6 +63,7 @@ LaunchFn make_gemm_tc(Context *ctx, const Spec &s, std::string &impl);  // tcgen
 bool gemm_tc_supports(const Spec &s, std::string &why);
 LaunchFn make_attention_simt(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_attention_tc(Context *ctx, const Spec &s, std::string &impl);
+LaunchFn make_attention_pair(Context *ctx, const Spec &s, std::string &impl);  // dim 128, CTA pairs
 LaunchFn make_elementwise_rtc(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl);  // fill, l2_flush
 LaunchFn make_cublas_gemm(Context *ctx, const Spec &s, std::string &impl);

@@ -378,6 +378,12 @@ extern "C" int jr_compile(void *handle, const char *spec_json, jr_kernel **out, 
                 if (s.dtype == jade::DType::F32) {
                     k->run = jade::make_attention_simt(ctx, s, k->impl);
                     k->path = "simt";
+                } else if (s.op == Op::AttentionOnline && s.dim == 128 && (s.causal ? s.seq >= 6144 : s.seq >= 2048)) {
+                    // CTA-pair kernel: faster once each pair streams enough key tiles to
+                    // amortise its per-tile set-up (measured on B200; the two-tile
+                    // kernel below wins for shorter causal rows)
+                    k->run = jade::make_attention_pair(ctx, s, k->impl);
+                    k->path = "tcgen05";
                 } else {
                     k->run = jade::make_attention_tc(ctx, s, k->impl);
                     k->path = "tcgen05";

@@ -96,3 +96,72 @@ def test_attention_uniform_rows_kat(rt):
     V = rt.download_f32(v).reshape(S, D).astype(np.float64)
     exp = np.cumsum(V, axis=0) / np.arange(1, S + 1)[:, None]
     assert np.abs(rt.download(o).reshape(S, D) - exp).max() < 3e-3
+
+
+# ---------------------------------------------------------------- CTA-pair kernel
+# Head dim 128 with long key ranges (non-causal S >= 2048, causal S >= 6144) runs
+# on the cta_group::2 kernel (attention_tc2.cu): S triple-buffered in TMEM, two
+# softmax warps per lane quarter on alternating key steps, speculative maxima.
+
+def pair_impl(kern):
+    return "pair" in kern.info.get("impl", "")
+
+
+@pytest.mark.parametrize("B,H,S,causal", [(1, 2, 2048, False), (1, 1, 2100, False), (2, 1, 2304, False),
+                                          (1, 1, 6144, True), (1, 1, 6200, True)],
+                         ids=["full2048", "full2100tail", "full2304", "causal6144", "causal6200tail"])
+def test_attention_pair_kernel(rt, B, H, S, causal):
+    D = 128
+    got, qf, kf, vf = run_attention(rt, B, H, S, D, causal, seed=S + 7)
+    kern = rt.compile({"op": "attention_online", "heads": H, "seq": S, "dim": D, "causal": causal, "dtype": "bf16", "batch": B})
+    assert pair_impl(kern), kern.info
+    rng = np.random.default_rng(S)
+    nrow = 512 if causal else 1024
+    bh = rng.integers(0, B * H, nrow)
+    # both CTAs of a pair, tile edges, the last (partial) tile and random rows
+    edges = [min(e, S - 1) for e in (0, 1, 127, 128, 255, 256, S - 1, S - 2, (S // 256) * 256, (S // 256) * 256 + 128)]
+    rows = np.concatenate([edges, rng.integers(0, S, nrow - len(edges))])
+    check(got, qf, kf, vf, S, D, causal, (bh, rows), True)
+
+
+@pytest.mark.parametrize("dtype,out_dtype", [("fp16", None), ("bf16", "fp32")])
+def test_attention_pair_kernel_dtypes(rt, dtype, out_dtype):
+    B, H, S, D = 1, 1, 2048, 128
+    got, qf, kf, vf = run_attention(rt, B, H, S, D, False, dtype, out_dtype, seed=5)
+    rows = np.arange(0, S, 3)
+    check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), (out_dtype or dtype) != "fp32")
+
+
+def test_attention_pair_kernel_rescales(rt):
+    # scores that grow along the keys force the running maximum up by far more
+    # than 2^8 at every key step: the speculative P is redone and O rescaled each step
+    B, H, S, D = 1, 1, 2048, 128
+    n = S * D
+    key = np.arange(S, dtype=np.float32)[:, None]
+    qh = np.ones((S, D), np.float32) * 0.5
+    kh = np.repeat(key * (0.04 / 0.5) / 8, D, axis=1).astype(np.float32)
+    vh = np.random.default_rng(9).standard_normal((S, D)).astype(np.float32)
+    bufs = [rt.alloc(n, "bf16") for _ in range(4)]
+    for b, h in zip(bufs[:3], (qh, kh, vh)):
+        rt.upload(b, jc.runtime.f32_to_bf16(h.ravel()))
+    kern = rt.compile({"op": "attention_online", "heads": H, "seq": S, "dim": D, "causal": False, "dtype": "bf16"})
+    assert pair_impl(kern), kern.info
+    rt.execute([(kern, bufs)])
+    got = rt.download_f32(bufs[3]).reshape(1, S, D)
+    qf, kf, vf = (rt.download_f32(b) for b in bufs[:3])
+    rows = np.arange(0, S, 7)
+    check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), True)
+
+
+def test_attention_pair_kernel_uniform_kat(rt):
+    # Q = K = 0: every non-causal output row is the mean of all V rows
+    B, H, S, D = 1, 1, 2048, 128
+    n = S * D
+    q, k, v, o = rt.alloc(n, "bf16"), rt.alloc(n, "bf16"), rt.alloc(n, "bf16"), rt.alloc(n, "fp32")
+    rt.fill(v, "normal", seed=2, lo=0.0, hi=1.0)
+    kern = rt.compile({"op": "attention_online", "heads": H, "seq": S, "dim": D, "causal": False, "dtype": "bf16",
+                       "out_dtype": "fp32"})
+    assert pair_impl(kern), kern.info
+    rt.execute([(kern, [q, k, v, o])])
+    V = rt.download_f32(v).reshape(S, D).astype(np.float64)
+    assert np.abs(rt.download(o).reshape(S, D) - V.mean(axis=0)[None]).max() < 2e-3
