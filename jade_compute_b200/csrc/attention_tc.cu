@@ -62,15 +62,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16.
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
 template <int D, typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -163,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // ------------------------------------- MMA issuer
+        {  // ------------------------------------- MMA issuer (whole warp, one elected lane issues)
             const uint32_t sq0 = smem_u32(smem + L::kQ);
             auto issue_s = [&](int t, int j) {
                 const uint32_t sq = sq0 + t * L::kTile, sk = smem_u32(smem + L::kK + (j & 1) * L::kTile);
@@ -181,8 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_ts(tmem_o[t], tmem_s[t] + k * 8, sdesc_sw128(sv + k * 16 * 128, L::kChunk, 1024), kIdescO, (j | k) != 0);
                 umma_commit(&o_full[t]);
             };
-            bool ok = nkv_max > 0 && mbar_wait(q_full, 0, abort_flag, err, kErrWaitTmaFull);
-            if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrWaitTmaFull);
+            bool ok = nkv_max > 0 && mbar_wait_warp(q_full, 0, abort_flag, err, kErrWaitTmaFull);
+            if (ok) ok = mbar_wait_warp(&k_full[0], 0, abort_flag, err, kErrWaitTmaFull);
             if (ok) {
                 tc_fence_after();
                 for (int t = 0; t < 2; ++t)
@@ -192,14 +183,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; ok && j < nkv_max; ++j) {
                 const bool more = j + 1 < nkv_max;
                 bool k_ready = false;
-                if (!(ok = mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
+                if (!(ok = mbar_wait_warp(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
                 for (int t = 0; t < 2 && ok; ++t) {
                     if (j >= nkv[t]) continue;
-                    if (!(ok = mbar_wait(&p_full[t], j & 1, abort_flag, err, kErrWaitProb))) break;
+                    if (!(ok = mbar_wait_warp(&p_full[t], j & 1, abort_flag, err, kErrWaitProb))) break;
                     tc_fence_after();
                     issue_pv(t, j);  // reads P_t(j) from TMEM: must precede S_t(j+1)
                     if (j + 1 < nkv[t]) {
-                        if (!k_ready && !(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
+                        if (!k_ready && !(ok = mbar_wait_warp(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
                         k_ready = true;
                         tc_fence_after();
                         issue_s(t, j + 1);  // overwrites S_t / P_t

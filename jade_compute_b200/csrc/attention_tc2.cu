@@ -20,16 +20,20 @@
 //
 //   warp 0     TMA producer (both CTAs): own Q rows once; own K/V halves into
 //              four-stage rings; completion is counted on CTA 0's barriers.
-//   warp 1     CTA 0: MMA issuer  S(0) S(1) S(2) | P(j).V(j) S(j+3) ...
-//              CTA 1: relays its softmax warps' "P(j) written" to CTA 0
-//   warps 2-9  softmax: warps w and w+4 share TMEM lane quarter w%4 and split
-//              each row's 128 keys in halves; they exchange half-row maxima per
-//              step through shared memory so both use the same running maximum.
-//              P(j) (16-bit pairs) is written over the half's own S columns.
-// O is rescaled in place only when a row maximum grows by more than 2^8; the
-// rescale first waits for P(j-1).V(j-1). A small fixed share of the exponentials
-// of unmasked tiles is evaluated with a cubic polynomial on the FMA pipe instead
-// of the MUFU unit, which is the softmax bottleneck.
+//   warp 1     CTA 0: MMA issuer  S(0) S(1) S(2) | P(j).V(j) S(j+3) ... (the whole
+//              warp runs the loop, one elected lane issues); CTA 1: relays its
+//              softmax warps' "P(j) written" to CTA 0 in one remote arrival.
+//   warps 2-9  softmax: warps w and w+4 share TMEM lane quarter w%4 and take the
+//              even and the odd key steps, one thread per query row. The running
+//              maximum is handed from step to step through shared memory; P(j) is
+//              computed speculatively with the last maximum seen and redone only
+//              if step j-1 moved it or row j's maximum grows by more than 2^8
+//              (then O is rescaled in place after P(j-1).V(j-1) has landed).
+//              P(j) (16-bit pairs) is written over the first 64 columns of S(j).
+// A small fixed share of the exponentials of unmasked tiles is evaluated with a
+// cubic polynomial on the FMA pipe instead of the MUFU unit.
+// Short waits poll (mbarrier.test_wait) instead of suspending: a suspended
+// waiter resumes a few hundred cycles after the phase completes.
 // Every wait is bounded (the error word records where it gave up); every thread
 // of both CTAs reaches the final cluster barrier, after which TMEM is released.
 #include <cuda.h>
@@ -47,7 +51,7 @@ namespace {
 constexpr int kRows = 128;     // query rows per CTA
 constexpr int kKeys = 128;     // keys per step
 constexpr int kDim = 128;      // head dim
-constexpr int kStages = 4;     // K and V ring depth
+constexpr int kStages = 3;     // K and V ring depth (V loads trail K by one step)
 // two softmax warps per TMEM lane quarter: one takes the even key steps, the
 // other the odd ones, each thread a whole row (128 scores) of its steps
 constexpr int kCols = kKeys;
@@ -57,22 +61,27 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kPolyPairs = 1;
 
 struct Layout {
-    static constexpr uint32_t kQ = 0;                 // 2 chunks x 16 KB (128 rows x 64 dims, SW128)
+    static constexpr uint32_t kQBuf = 32768;          // 2 chunks x 16 KB (128 rows x 64 dims, SW128)
     static constexpr uint32_t kKStage = 16384;        // 2 chunks x 8 KB (64 keys x 64 dims)
     static constexpr uint32_t kVStage = 16384;        // 128 keys x 64 dims
-    static constexpr uint32_t kK = kQ + 32768;
+    static constexpr uint32_t kQ = 0;                 // two Q buffers: the next work item's Q loads early
+    static constexpr uint32_t kK = kQ + 2 * kQBuf;
     static constexpr uint32_t kV = kK + kStages * kKStage;
-    // never written: keeps any operand window that a descriptor could describe
-    // past the last V stage inside the allocation
-    static constexpr uint32_t kGuard = kV + kStages * kVStage;
-    static constexpr uint32_t kBar = kGuard + 32768;
-    static constexpr uint32_t kRed = kBar + 512;      // float [2][128] running maxima, [2][128] row sums
-    static constexpr uint32_t kSmem = kRed + 2 * 2 * 128 * 4 + 1024;
+    // O staging for the TMA store of 16-bit outputs: two halves of 64 columns
+    // (128 rows x 128 B, 128-byte swizzle), one per softmax warp parity
+    static constexpr uint32_t kO = kV + kStages * kVStage;
+    static constexpr uint32_t kBar = kO + 2 * 16384;
+    // floats: running-maximum tokens [2][128]; per work item (double-buffered)
+    // final maxima [2][2][128] and row sums [2][2][128]
+    static constexpr uint32_t kRed = kBar + 512;
+    static constexpr uint32_t kSmem = kRed + (256 + 512 + 512) * 4 + 1024;
 };
 
 struct Args {
     void *out;
     int seq, nq_tiles, npairs, nkv_tiles, causal;
+    int bh_total;  // batch * heads
+    int clusters;  // CTA pairs launched; pair c takes work items c, c + clusters, ...
     float scale_log2;
     int *err;
 };
@@ -135,6 +144,17 @@ __device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
 }
+// TMA tile store from this CTA's shared memory (rows beyond the tensor are clipped).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int32_t c0, int32_t c1, int32_t c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// this thread's bulk stores have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's bulk stores are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
 }
@@ -274,10 +294,35 @@ __device__ __forceinline__ float store_p(const float (&sv)[kCols], float c, floa
     return (a0 + a1) + (b0 + b1);
 }
 
+// This thread's row of an S tile (keys k0..k0+127) from TMEM into sv, causal and
+// tail masks applied as -inf; returns the row maximum times c.
+__device__ __forceinline__ float load_row_max(float (&sv)[kCols], uint32_t ts, int k0, int q0, int q, int seq, int causal, float c) {
+    tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < kCols; cc += 32) tmem_ld32f(ts + cc, sv + cc);
+    tmem_wait_ld();
+    reg_fence(sv);
+    if ((causal && k0 + kKeys - 1 > q0) || (k0 + kKeys > seq)) {  // keys k0 + i with i > lim are invisible
+        const int lim = min(seq - 1, causal ? q : INT_MAX) - k0;
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) sv[i] = i <= lim ? sv[i] : -INFINITY;
+    }
+    float mx[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[e + 8], sv[e + 16]);
+#pragma unroll
+    for (int i = 24; i < kCols - 8; i += 16)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kCols - 8 + e]);
+    return max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * c;
+}
+
 template <typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, const Args args) {
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const Args args) {
     using L = Layout;
     constexpr uint32_t kFmt = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
     constexpr uint32_t kIdescS = idesc_f32acc(kFmt, kFmt, false, false, 2 * kRows, kKeys);
@@ -286,45 +331,65 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBar);
-    uint64_t *q_full = bars + 0;
-    uint64_t *k_full = bars + 1, *k_empty = bars + 5, *v_full = bars + 9, *v_empty = bars + 13;  // [stage]
-    uint64_t *s_full = bars + 17, *p_full = bars + 20;                                         // [S buffer]
-    // P(j).V(j) done, for the O rescale: S(j+3) in general (issued right behind it);
-    // o_tail[0], o_tail[1] for the last two steps, o_last for the final one
-    uint64_t *o_tail = bars + 23, *o_last = bars + 25;
-    uint64_t *pub = bars + 26;  // [lane quarter][step parity]: running maximum after a step published
-    uint64_t *fin = bars + 34;  // [lane quarter]: both warps' final maxima and sums posted
-    uint64_t *mma_done = bars + 38;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 39);
+    uint64_t *q_full = bars + 0, *q_empty = bars + 2;                                        // [Q buffer]
+    uint64_t *k_full = bars + 4, *k_empty = bars + 8, *v_full = bars + 12, *v_empty = bars + 16;  // [stage]
+    uint64_t *s_full = bars + 20, *p_full = bars + 23;                                       // [S buffer]
+    // P(g).V(g) done, for the O rescale: S(g+3) in general (issued right behind
+    // it); o_tail[0], o_tail[1] for this pair's last two key steps
+    uint64_t *o_tail = bars + 26;
+    uint64_t *o_last = bars + 28;  // per work item: its last P.V done (O complete)
+    uint64_t *o_free = bars + 29;  // per work item: O read out by both CTAs (next item may overwrite)
+    uint64_t *pub = bars + 30;     // [lane quarter][step parity]: running maximum after a step published
+    uint64_t *fin = bars + 38;     // [lane quarter]: both warps' final maxima and sums posted
+    uint64_t *mma_done = bars + 42;
+    uint64_t *stg_empty = bars + 43, *stg_full = bars + 45;  // [warp parity]: O staging free / written
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 47);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    float *red = reinterpret_cast<float *>(smem + L::kRed);  // [2][2][128]
+    float *tok = reinterpret_cast<float *>(smem + L::kRed);  // [2][128]
+    float *fin_m = tok + 256, *fin_l = tok + 768;             // [2 items][2 warps][128]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
-    const int bh = blockIdx.y;
-    const int pair = args.npairs - 1 - (int)blockIdx.z;  // heaviest causal pairs first
-    const int q0 = (2 * pair + (int)rank) * kRows;
-    const int nsteps = args.causal ? min(2 * pair + 2, args.nkv_tiles) : args.nkv_tiles;
+    const int cluster = blockIdx.x >> 1;
+    const int total_items = args.bh_total * args.npairs;
+    // work item it: heaviest causal pairs first, all heads of a pair index together
+    auto item_bh = [&](int it) { return it % args.bh_total; };
+    auto item_pair = [&](int it) { return args.npairs - 1 - it / args.bh_total; };
+    auto item_steps = [&](int it) {
+        const int p = item_pair(it);
+        return args.causal ? min(2 * p + 2, args.nkv_tiles) : args.nkv_tiles;
+    };
+    // this pair's k-th work item: boustrophedon over the heavy-first order (round k
+    // runs the pairs forward for even k, backward for odd k), which balances the
+    // causal triangle to within a few percent; -1 when the pair has no k-th item
+    auto item_of = [&](int k) {
+        const int it = k * args.clusters + ((k & 1) ? args.clusters - 1 - cluster : cluster);
+        return it < total_items ? it : -1;
+    };
+    int total_steps = 0;  // key steps over all of this pair's work items
+    for (int k = 0, it; (it = item_of(k)) >= 0; ++k) total_steps += item_steps(it);
     int *err = args.err;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
+        for (int b = 0; b < 2; ++b) { mbar_init(&q_full[b], 1); mbar_init(&q_empty[b], 1); }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
             mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1);
         }
         for (int b = 0; b < 3; ++b) {
             mbar_init(&s_full[b], 1);
-            // CTA 0: its softmax warps + one forwarded arrival for CTA 1's softmax warps
+            // CTA 0: its 4 step-owning softmax warps + one relayed arrival for CTA 1's
             mbar_init(&p_full[b], 4 + (leader ? 1 : 0));
         }
         mbar_init(&o_tail[0], 1);
         mbar_init(&o_tail[1], 1);
         mbar_init(o_last, 1);
+        mbar_init(o_free, 8 + (leader ? 1 : 0));
         for (int q = 0; q < 8; ++q) mbar_init(&pub[q], 32);
         for (int q = 0; q < 4; ++q) mbar_init(&fin[q], 64);
         mbar_init(mma_done, 1);
+        for (int p = 0; p < 2; ++p) { mbar_init(&stg_empty[p], 1); mbar_init(&stg_full[p], 128); }
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -343,251 +408,302 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            const uint32_t q_full_lead = map_rank(smem_u32(q_full), 0);
-            if (leader) mbar_arrive_expect_tx(q_full, 2 * 32768);
-            for (int c = 0; c < 2; ++c) tma_load_3d_pair(smem + L::kQ + c * 16384, &tmQ, q_full_lead, c * 64, q0, bh);
-            int issued = 0;
-            for (int j = 0; j < nsteps && !*abort_flag; ++j) {
-                const int st = j % kStages;
-                const uint32_t ph = (j / kStages) & 1;
-                if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
-                if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * L::kKStage);
-                const uint32_t kf = map_rank(smem_u32(&k_full[st]), 0);
-                for (int c = 0; c < 2; ++c)
-                    tma_load_3d_pair(smem + L::kK + st * L::kKStage + c * 8192, &tmK, kf, c * 64, j * kKeys + (int)rank * 64, bh);
-                if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
-                if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * L::kVStage);
-                tma_load_3d_pair(smem + L::kV + st * L::kVStage, &tmV, map_rank(smem_u32(&v_full[st]), 0), (int)rank * 64, j * kKeys, bh);
-                issued = j + 1;
+            int g = 0, k = 0, q_issued = 0, k_issued = 0, v_issued = 0;
+            bool ok = true;
+            for (int it; ok && (it = item_of(k)) >= 0; ++k) {
+                const int bh = item_bh(it), n = item_steps(it), q0 = (2 * item_pair(it) + (int)rank) * kRows, qb = k & 1;
+                if (!(ok = mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1, abort_flag, err, kErrWaitSmemEmpty))) break;
+                if (leader) mbar_arrive_expect_tx(&q_full[qb], 2 * L::kQBuf);
+                const uint32_t qf = map_rank(smem_u32(&q_full[qb]), 0);
+                for (int c = 0; c < 2; ++c) tma_load_3d_pair(smem + L::kQ + qb * L::kQBuf + c * 16384, &tmQ, qf, c * 64, q0, bh);
+                q_issued = k + 1;
+                // K(g) then V(g-1): a K load never queues behind a V stage that P.V still reads
+                for (int j = 0; j <= n && ok; ++j) {
+                    if (j < n) {
+                        const int gk = g + j, st = gk % kStages;
+                        if (!(ok = mbar_wait(&k_empty[st], ((gk / kStages) & 1) ^ 1, abort_flag, err, kErrWaitSmemEmpty))) break;
+                        if (leader) mbar_arrive_expect_tx(&k_full[st], 2 * L::kKStage);
+                        const uint32_t kf = map_rank(smem_u32(&k_full[st]), 0);
+                        for (int c = 0; c < 2; ++c)
+                            tma_load_3d_pair(smem + L::kK + st * L::kKStage + c * 8192, &tmK, kf, c * 64, j * kKeys + (int)rank * 64, bh);
+                        k_issued = gk + 1;
+                    }
+                    if (j > 0) {
+                        const int gv = g + j - 1, st = gv % kStages;
+                        if (!(ok = mbar_wait(&v_empty[st], ((gv / kStages) & 1) ^ 1, abort_flag, err, kErrWaitSmemEmpty))) break;
+                        if (leader) mbar_arrive_expect_tx(&v_full[st], 2 * L::kVStage);
+                        tma_load_3d_pair(smem + L::kV + st * L::kVStage, &tmV, map_rank(smem_u32(&v_full[st]), 0), (int)rank * 64,
+                                         (j - 1) * kKeys, bh);
+                        v_issued = gv + 1;
+                    }
+                }
+                g += n;
             }
             if (*abort_flag && leader) {  // CTA 0 counts both CTAs' copies: wait for those still in flight
-                mbar_wait_drain(q_full, 0, err);
-                for (int j = max(0, issued - kStages); j < issued; ++j) {
-                    mbar_wait_drain(&k_full[j % kStages], (j / kStages) & 1, err);
-                    mbar_wait_drain(&v_full[j % kStages], (j / kStages) & 1, err);
-                }
+                for (int kk = max(0, q_issued - 2); kk < q_issued; ++kk) mbar_wait_drain(&q_full[kk & 1], (kk >> 1) & 1, err);
+                for (int gg = max(0, k_issued - kStages); gg < k_issued; ++gg) mbar_wait_drain(&k_full[gg % kStages], (gg / kStages) & 1, err);
+                for (int gg = max(0, v_issued - kStages); gg < v_issued; ++gg) mbar_wait_drain(&v_full[gg % kStages], (gg / kStages) & 1, err);
             }
         }
     } else if (warp == 1) {
         if (leader) {  // ------------------------------- MMA issuer (CTA 0, whole warp, one elected lane issues)
-            const uint32_t sq = smem_u32(smem + L::kQ);
             auto commit_both = [&](uint64_t *bar) {
                 umma_commit_pair(smem_u32(bar));
                 umma_commit_pair(map_rank(smem_u32(bar), 1));
             };
             // polling waits: a suspended waiter resumes a few hundred cycles after
-            // the phase completes, and this warp waits three times per key step
+            // the phase completes, and this warp waits several times per key step
             auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
                 return __all_sync(0xffffffffu, mbar_spin(bar, parity, abort_flag, err, code));
             };
-            bool ok = wait(q_full, 0, kErrWaitTmaFull);
-            auto issue_s = [&](int j, bool wait_k) {  // S(j) = Q K_j^T into buffer j % 3
-                const int st = j % kStages;
-                if (wait_k && !wait(&k_full[st], (j / kStages) & 1, kErrWaitTmaFull)) return false;
+            // S issue cursor: work item (index it, sequence number k, n steps), local step j
+            int s_k = 0, s_j = 0, s_n = item_of(0) >= 0 ? item_steps(item_of(0)) : 0;
+            auto issue_s = [&](int gs, bool wait_inputs) {  // S(gs) = Q K^T into buffer gs % 3
+                const int st = gs % kStages, qb = s_k & 1;
+                if (wait_inputs) {
+                    if (s_j == 0 && !wait(&q_full[qb], (s_k >> 1) & 1, kErrWaitTmaFull)) return false;
+                    if (!wait(&k_full[st], (gs / kStages) & 1, kErrWaitTmaFull)) return false;
+                }
                 tc_fence_after();
+                const uint32_t sq = smem_u32(smem + L::kQ + qb * L::kQBuf);
                 const uint32_t sk = smem_u32(smem + L::kK + st * L::kKStage);
 #pragma unroll
                 for (int k = 0; k < kDim / 16; ++k)
-                    umma_pair_ss(tmem + (j % 3) * 128, sdesc_sw128(sq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                    umma_pair_ss(tmem + (gs % 3) * 128, sdesc_sw128(sq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
                                  sdesc_sw128(sk + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024), kIdescS, k != 0);
-                commit_both(&s_full[j % 3]);
+                commit_both(&s_full[gs % 3]);
                 commit_both(&k_empty[st]);
+                if (s_j == s_n - 1) commit_both(&q_empty[qb]);  // the item's last S: its Q buffer is free
+                if (++s_j == s_n) {
+                    s_j = 0;
+                    ++s_k;
+                    const int nx = item_of(s_k);
+                    s_n = nx >= 0 ? item_steps(nx) : 0;
+                }
                 return true;
             };
-            for (int j = 0; ok && j < 3 && j < nsteps; ++j) ok = issue_s(j, true);
-            for (int j = 0; ok && j < nsteps; ++j) {
-                const int st = j % kStages, st3 = (j + 3) % kStages;
-                const bool more = j + 3 < nsteps;
-                // this step's inputs (P(j), V(j), K(j+3)) are tested together so the
-                // barrier latencies overlap; the bounded waits run only if one is missing
-                const bool rp = mbar_test_wait(&p_full[j % 3], (j / 3) & 1);
-                const bool rv = mbar_test_wait(&v_full[st], (j / kStages) & 1);
-                const bool rk = !more || mbar_test_wait(&k_full[st3], ((j + 3) / kStages) & 1);
-                if (!__all_sync(0xffffffffu, rp && rv && rk)) {
-                    if (!(ok = wait(&p_full[j % 3], (j / 3) & 1, kErrWaitProb))) break;
-                    if (!(ok = wait(&v_full[st], (j / kStages) & 1, kErrWaitTmaFull))) break;
-                    if (more && !(ok = wait(&k_full[st3], ((j + 3) / kStages) & 1, kErrWaitTmaFull))) break;
+            bool ok = true;
+            for (int gs = 0; ok && gs < 3 && gs < total_steps; ++gs) ok = issue_s(gs, true);
+            int p_k = 0, p_j = 0, p_n = item_of(0) >= 0 ? item_steps(item_of(0)) : 0;
+            for (int g = 0; ok && g < total_steps; ++g) {
+                const int st = g % kStages;
+                const bool more = g + 3 < total_steps;
+                const bool first = p_j == 0 && p_k > 0;  // O still holds the previous item until it is read out
+                // this step's inputs (P(g), V(g), K(g+3), Q of S(g+3)'s item, O free)
+                // are tested together so the barrier latencies overlap; the bounded
+                // waits run only if one is missing
+                bool r = mbar_test_wait(&p_full[g % 3], (g / 3) & 1);
+                r &= mbar_test_wait(&v_full[st], (g / kStages) & 1);
+                if (more) r &= mbar_test_wait(&k_full[(g + 3) % kStages], ((g + 3) / kStages) & 1);
+                if (more && s_j == 0) r &= mbar_test_wait(&q_full[s_k & 1], (s_k >> 1) & 1);
+                if (first) r &= mbar_test_wait(o_free, (p_k - 1) & 1);
+                if (!__all_sync(0xffffffffu, r)) {
+                    if (!(ok = wait(&p_full[g % 3], (g / 3) & 1, kErrWaitProb))) break;
+                    if (!(ok = wait(&v_full[st], (g / kStages) & 1, kErrWaitTmaFull))) break;
+                    if (more && !(ok = wait(&k_full[(g + 3) % kStages], ((g + 3) / kStages) & 1, kErrWaitTmaFull))) break;
+                    if (more && s_j == 0 && !(ok = wait(&q_full[s_k & 1], (s_k >> 1) & 1, kErrWaitTmaFull))) break;
+                    if (first && !(ok = wait(o_free, (p_k - 1) & 1, kErrWaitPv))) break;
                 }
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + L::kV + st * L::kVStage);
-                const uint32_t sp = tmem + (j % 3) * 128;
+                const uint32_t sp = tmem + (g % 3) * 128;
 #pragma unroll
                 for (int k = 0; k < kKeys / 16; ++k)  // keys 16k..16k+15: P columns 8k..8k+7
-                    umma_pair_ts(tmem_o, sp + k * 8, sdesc_sw128(sv + k * 2048, 16384, 1024), kIdescO,
-                                 (j | k) != 0);
+                    umma_pair_ts(tmem_o, sp + k * 8, sdesc_sw128(sv + k * 2048, 16384, 1024), kIdescO, (p_j | k) != 0);
                 commit_both(&v_empty[st]);
-                if (j == nsteps - 3) commit_both(&o_tail[0]);
-                if (j == nsteps - 2) commit_both(&o_tail[1]);
-                if (j == nsteps - 1) commit_both(o_last);
-                if (more) issue_s(j + 3, false);  // reuses P(j)'s buffer: after P(j).V(j) in issue order
+                if (g == total_steps - 3) commit_both(&o_tail[0]);
+                if (g == total_steps - 2) commit_both(&o_tail[1]);
+                if (p_j == p_n - 1) commit_both(o_last);
+                if (more) issue_s(g + 3, false);  // reuses P(g)'s buffer: after P(g).V(g) in issue order
+                if (++p_j == p_n) {
+                    p_j = 0;
+                    ++p_k;
+                    const int nx = item_of(p_k);
+                    p_n = nx >= 0 ? item_steps(nx) : 0;
+                }
             }
             umma_commit_pair(smem_u32(mma_done));
             mbar_wait_drain(mma_done, 0, err);
-        } else if (lane == 0) {  // --------------------------- P forwarder (CTA 1)
-            // One remote arrival per step instead of one per softmax warp: an
-            // arrival on the peer's barrier stalls the arriving warp for hundreds
-            // of cycles, so the softmax warps arrive locally and this thread relays.
-            for (int j = 0; j < nsteps; ++j) {
-                if (!mbar_spin(&p_full[j % 3], (j / 3) & 1, abort_flag, err, kErrWaitProb)) break;
-                tc_fence_after();
-                tc_fence_before();
-                mbar_arrive_remote(map_rank(smem_u32(&p_full[j % 3]), 0));
+        } else if (lane == 0) {  // --------------------------- relay (CTA 1)
+            // One remote arrival per event instead of one per softmax warp: the
+            // softmax warps arrive locally and this thread relays, in the order the
+            // events happen: P(g) for the steps of a work item, then O read out.
+            int g = 0, k = 0;
+            bool ok = true;
+            for (int it; ok && (it = item_of(k)) >= 0; ++k) {
+                const int n = item_steps(it);
+                for (int j = 0; j < n; ++j, ++g) {
+                    if (!(ok = mbar_spin(&p_full[g % 3], (g / 3) & 1, abort_flag, err, kErrWaitProb))) break;
+                    tc_fence_after();
+                    tc_fence_before();
+                    mbar_arrive_remote(map_rank(smem_u32(&p_full[g % 3]), 0));
+                }
+                if (ok && (ok = mbar_wait(o_free, k & 1, abort_flag, err, kErrWaitPv))) {
+                    tc_fence_after();
+                    tc_fence_before();
+                    mbar_arrive_remote(map_rank(smem_u32(o_free), 0));
+                }
             }
         }
     } else {
         // ----------------------------------------------------- softmax (warps 2-9, both CTAs)
         // Warp pair (w, w + 4) shares lane quarter w % 4: warp parity p = (w - 2) / 4
-        // takes steps j = p, p + 2, ... with one thread per row. The running
-        // maximum m is passed along the steps through shared memory: step j's
-        // owner computes P(j) with the maximum it last saw, then reads step j-1's
-        // published maximum; if that moved, it redoes P(j) (and rescales its row
-        // sum). If the row maximum grows by more than 2^8 it raises m, redoes P(j)
-        // and rescales O after P(j-1).V(j-1) has landed. Consecutive steps of the
-        // two warps overlap, so one computes while the other waits.
+        // takes the key steps g = p, p + 2, ... (counted over all work items), one
+        // thread per row. Within a work item the running maximum m is passed along
+        // the steps through shared memory: step g's owner computes P(g) with the
+        // maximum it last saw, then reads step g-1's published maximum; if that moved
+        // it redoes P(g) (and rescales its row sum). If the row maximum grows by more
+        // than 2^8 it raises m, redoes P(g) and rescales O after P(g-1).V(g-1) has
+        // landed. Consecutive steps of the two warps overlap, so one computes while
+        // the other waits. After an item's steps both warps combine their row sums,
+        // normalise and store half of O each, and release O for the next item.
         const int quarter = warp & 3;
         const int par = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
-        const int q = q0 + row;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         const float c = args.scale_log2;
-        float *tok = red;  // [2][128]: running maximum after the last step of each parity
-        float m_view = -INFINITY, l_own = 0.0f;  // l_own is in the scale of m_view
         bool ok = true;
-        for (int j = par; ok && j < nsteps; j += 2) {
-            const int b = j % 3;
-            const uint32_t ts = tmem + b * 128 + lane_off;
-            ok = __all_sync(0xffffffffu, mbar_spin(&s_full[b], (j / 3) & 1, abort_flag, err, kErrWaitScore));
-            if (!ok) break;
-            tc_fence_after();
-            float sv[kCols];
-#pragma unroll
-            for (int cc = 0; cc < kCols; cc += 32) tmem_ld32f(ts + cc, sv + cc);
-            tmem_wait_ld();
-            reg_fence(sv);
-            const int k0 = j * kKeys;
-            const bool need_mask = (args.causal && k0 + kKeys - 1 > q0) || (k0 + kKeys > args.seq);
-            if (need_mask) {  // keys k0 + i with i > lim are invisible to this row
-                const int lim = min(args.seq - 1, args.causal ? q : INT_MAX) - k0;
-#pragma unroll
-                for (int i = 0; i < kCols; ++i) sv[i] = i <= lim ? sv[i] : -INFINITY;
-            }
-            float mx[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[e + 8], sv[e + 16]);
-#pragma unroll
-            for (int i = 24; i < kCols - 8; i += 16)
-#pragma unroll
-                for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[kCols - 8 + e]);
-            const float m_tile = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * c;
-            // the maximum published by step j-1 (its owner is the other warp of the pair)
-            auto read_prev = [&]() {
-                if (!__all_sync(0xffffffffu, mbar_spin(&pub[quarter * 2 + (par ^ 1)], ((j - 1) >> 1) & 1, abort_flag, err, kErrWaitScore)))
-                    return false;
-                const float m_prev = tok[(par ^ 1) * 128 + row];
-                if (m_prev != m_view) {  // the other warp raised m since this warp's last step
-                    l_own *= m_view == -INFINITY ? 0.0f : mufu_exp2(m_view - m_prev);
-                    m_view = m_prev;
+        int g0 = 0, k = 0;
+        for (int it; ok && (it = item_of(k)) >= 0; ++k) {
+            const int bh = item_bh(it), n = item_steps(it), q0 = (2 * item_pair(it) + (int)rank) * kRows, q = q0 + row;
+            float m_view = -INFINITY, l_own = 0.0f;  // l_own is in the scale of m_view
+            for (int j = (par + g0) & 1; ok && j < n; j += 2) {
+                const int g = g0 + j, b = g % 3;
+                const uint32_t ts = tmem + b * 128 + lane_off;
+                // the item's first two steps start from the maximum over both of their
+                // tiles, computed by both warps alike, so neither waits for the other
+                float sv[kCols];
+                float m_pre = -INFINITY;
+                if (j <= 1 && n >= 2) {
+                    const int go = g0 + (j ^ 1);
+                    if (!(ok = __all_sync(0xffffffffu, mbar_spin(&s_full[go % 3], (go / 3) & 1, abort_flag, err, kErrWaitScore))))
+                        break;
+                    m_pre = load_row_max(sv, tmem + (go % 3) * 128 + lane_off, (j ^ 1) * kKeys, q0, q, args.seq, args.causal, c);
                 }
-                return true;
-            };
-            float psum = 0.0f;
-            bool fresh = false;  // P(j) in TMEM was computed with the current m_view
-            if (j == 0) {
-                m_view = m_tile;
-            } else if (m_view == -INFINITY) {  // first step of the odd warp: nothing to speculate with
-                if (!(ok = read_prev())) break;
-            } else {
-                const float m_spec = m_view;
-                psum = need_mask ? store_p<kFmt, false>(sv, c, m_spec, ts) : store_p<kFmt, kFmt == 1>(sv, c, m_spec, ts);
-                if (!(ok = read_prev())) break;
-                fresh = __all_sync(0xffffffffu, m_view == m_spec);
-            }
-            float alpha = 1.0f;
-            if (j > 0 && __any_sync(0xffffffffu, m_tile > m_view + kRescaleThreshold)) {
-                if (m_tile > m_view + kRescaleThreshold) {
-                    alpha = mufu_exp2(m_view - m_tile);
-                    m_view = m_tile;
+                if (!(ok = __all_sync(0xffffffffu, mbar_spin(&s_full[b], (g / 3) & 1, abort_flag, err, kErrWaitScore)))) break;
+                const float m_tile = load_row_max(sv, ts, j * kKeys, q0, q, args.seq, args.causal, c);
+                const int k0 = j * kKeys;
+                const bool need_mask = (args.causal && k0 + kKeys - 1 > q0) || (k0 + kKeys > args.seq);
+                // the maximum published by step g-1 of this item (the other warp's)
+                auto read_prev = [&]() {
+                    if (!__all_sync(0xffffffffu, mbar_spin(&pub[quarter * 2 + (par ^ 1)], ((g - 1) >> 1) & 1, abort_flag, err, kErrWaitScore)))
+                        return false;
+                    const float m_prev = tok[(par ^ 1) * 128 + row];
+                    if (m_prev != m_view) {  // the other warp raised m since this warp's last step
+                        l_own *= m_view == -INFINITY ? 0.0f : mufu_exp2(m_view - m_prev);
+                        m_view = m_prev;
+                    }
+                    return true;
+                };
+                float psum = 0.0f;
+                bool fresh = false;  // P(g) in TMEM was computed with the current m_view
+                if (j == 0) {
+                    m_view = fmaxf(m_tile, m_pre);
+                } else {
+                    if (j == 1) m_view = fmaxf(m_tile, m_pre);  // equals what step 0 publishes
+                    const float m_spec = m_view;
+                    psum = need_mask ? store_p<kFmt, false>(sv, c, m_spec, ts) : store_p<kFmt, kFmt == 1>(sv, c, m_spec, ts);
+                    if (!(ok = read_prev())) break;
+                    fresh = __all_sync(0xffffffffu, m_view == m_spec);
                 }
-                fresh = false;
-                // O (in TMEM) to the new maxima once P(j-1).V(j-1) has landed: S(j+2)
-                // was issued right behind it (its next phase needs P(j+2) from this
-                // warp, so the wait cannot alias); the last two steps have o_tail.
-                if (j + 2 < nsteps)
-                    ok = __all_sync(0xffffffffu, mbar_wait(&s_full[(j + 2) % 3], ((j + 2) / 3) & 1, abort_flag, err, kErrWaitPv));
-                else
-                    ok = __all_sync(0xffffffffu, mbar_wait(&o_tail[j + 2 - nsteps], 0, abort_flag, err, kErrWaitPv));
-                if (!ok) break;
-                tc_fence_after();
+                float alpha = 1.0f;
+                if (j > 0 && __any_sync(0xffffffffu, m_tile > m_view + kRescaleThreshold)) {
+                    if (m_tile > m_view + kRescaleThreshold) {
+                        alpha = mufu_exp2(m_view - m_tile);
+                        m_view = m_tile;
+                    }
+                    fresh = false;
+                    // O (in TMEM) to the new maxima once P(g-1).V(g-1) has landed: S(g+2)
+                    // was issued right behind it (its next phase needs P(g+2) from this
+                    // warp, so the wait cannot alias); the last two steps have o_tail.
+                    if (g + 2 < total_steps)
+                        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[(g + 2) % 3], ((g + 2) / 3) & 1, abort_flag, err, kErrWaitPv));
+                    else
+                        ok = __all_sync(0xffffffffu, mbar_wait(&o_tail[g + 2 - total_steps], 0, abort_flag, err, kErrWaitPv));
+                    if (!ok) break;
+                    tc_fence_after();
 #pragma unroll 1
-                for (int oc = 0; oc < kDim; oc += 32) {
-                    float ov[32];
-                    tmem_ld32f(tmem_o + lane_off + oc, ov);
-                    tmem_wait_ld();
+                    for (int oc = 0; oc < kDim; oc += 32) {
+                        float ov[32];
+                        tmem_ld32f(tmem_o + lane_off + oc, ov);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-                    tmem_st32f(tmem_o + lane_off + oc, ov);
+                        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                        tmem_st32f(tmem_o + lane_off + oc, ov);
+                    }
+                    l_own *= alpha;
                 }
-                l_own *= alpha;
+                if (!fresh) psum = store_p<kFmt, false>(sv, c, m_view, ts);
+                l_own += psum;
+                // publish the running maximum after step g for the owner of step g+1
+                tok[par * 128 + row] = m_view;
+                mbar_arrive(&pub[quarter * 2 + par]);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[b]);
             }
-            if (!fresh) psum = store_p<kFmt, false>(sv, c, m_view, ts);
-            l_own += psum;
-            // publish the running maximum after step j for the owner of step j+1
-            tok[par * 128 + row] = m_view;
-            mbar_arrive(&pub[quarter * 2 + par]);
-            tmem_wait_st();
+            if (!ok) break;
+            // row sum: both warps' sums brought to the final (largest) maximum
+            float *fm = fin_m + (k & 1) * 256, *fl = fin_l + (k & 1) * 256;
+            fm[par * 128 + row] = m_view;
+            fl[par * 128 + row] = l_own;
+            mbar_arrive(&fin[quarter]);
+            ok = __all_sync(0xffffffffu, mbar_spin(&fin[quarter], k & 1, abort_flag, err, kErrWaitScore));
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_last, k & 1, abort_flag, err, kErrWaitPv));
+            if (!ok) break;
+            const float m_other = fm[(par ^ 1) * 128 + row], l_other = fl[(par ^ 1) * 128 + row];
+            const float m_final = fmaxf(m_view, m_other);
+            const float l_row = (l_own > 0.0f ? l_own * mufu_exp2(m_view - m_final) : 0.0f) +
+                                (l_other > 0.0f ? l_other * mufu_exp2(m_other - m_final) : 0.0f);
+            const float inv = 1.0f / l_row;
+            tc_fence_after();
+            // this warp's half of the row's output columns, then O is free for the next item
+            float r[64];
+            tmem_ld32f(tmem_o + lane_off + par * 64, r);
+            tmem_ld32f(tmem_o + lane_off + par * 64 + 32, r + 32);
+            tmem_wait_ld();
+            reg_fence(r);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[b]);
-        }
-        if (ok && nsteps > 0) {
-            // row sum: both warps' sums brought to the final (largest) maximum;
-            // a warp's last publication equals its m_view, a warp without steps has -inf
-            float *lsum = red + 256;  // [2][128]
-            tok[par * 128 + row] = m_view;
-            lsum[par * 128 + row] = l_own;
-            mbar_arrive(&fin[quarter]);
-            ok = __all_sync(0xffffffffu, mbar_spin(&fin[quarter], 0, abort_flag, err, kErrWaitScore));
-            float l_row = 0.0f;
-            if (ok) {
-                const float m_other = tok[(par ^ 1) * 128 + row], l_other = lsum[(par ^ 1) * 128 + row];
-                const float m_final = fmaxf(m_view, m_other);
-                l_row = (l_own > 0.0f ? l_own * mufu_exp2(m_view - m_final) : 0.0f) +
-                        (l_other > 0.0f ? l_other * mufu_exp2(m_other - m_final) : 0.0f);
-            }
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_last, 0, abort_flag, err, kErrWaitPv));
-            if (ok) {
-                const float inv = 1.0f / l_row;
-                tc_fence_after();
-                // each warp of the pair writes half of the row's output columns
-                TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * kDim + par * 64;
-#pragma unroll 1
-                for (int oc = 0; oc < 64; oc += 32) {
-                    float r[32];
-                    tmem_ld32f(tmem_o + lane_off + par * 64 + oc, r);
-                    tmem_wait_ld();
-                    if (q < args.seq) {
+            if (lane == 0) mbar_arrive(o_free);
+            if constexpr (std::is_same<TOut, float>::value) {
+                float *o = static_cast<float *>(args.out) + ((size_t)bh * args.seq + q) * kDim + par * 64;
+                if (q < args.seq)
 #pragma unroll
-                        for (int e = 0; e < 32; e += 8) {
-                            if constexpr (std::is_same<TOut, float>::value) {
-                                *reinterpret_cast<float4 *>(o + oc + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
-                                *reinterpret_cast<float4 *>(o + oc + e + 4) =
-                                    make_float4(r[e + 4] * inv, r[e + 5] * inv, r[e + 6] * inv, r[e + 7] * inv);
-                            } else {
-                                uint4 u;
-                                u.x = pack16<kFmt>(r[e] * inv, r[e + 1] * inv);
-                                u.y = pack16<kFmt>(r[e + 2] * inv, r[e + 3] * inv);
-                                u.z = pack16<kFmt>(r[e + 4] * inv, r[e + 5] * inv);
-                                u.w = pack16<kFmt>(r[e + 6] * inv, r[e + 7] * inv);
-                                *reinterpret_cast<uint4 *>(o + oc + e) = u;
-                            }
-                        }
-                    }
+                    for (int e = 0; e < 64; e += 4) *reinterpret_cast<float4 *>(o + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
+            } else {
+                // staged in shared memory (128-byte swizzle, the tensor map's layout) and
+                // written by one TMA store per half: coalesced, and rows past seq are clipped
+                const bool issuer = warp == 2 + 4 * par && lane == 0;
+                uint8_t *stg = smem + L::kO + par * 16384;
+                if (issuer) {  // the previous item's store has finished reading the staging buffer
+                    bulk_wait_read_all();
+                    mbar_arrive(&stg_empty[par]);
+                }
+                ok = __all_sync(0xffffffffu, mbar_spin(&stg_empty[par], k & 1, abort_flag, err, kErrWaitPv));
+                if (!ok) break;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    uint4 u;
+                    u.x = pack16<kFmt>(r[8 * ch] * inv, r[8 * ch + 1] * inv);
+                    u.y = pack16<kFmt>(r[8 * ch + 2] * inv, r[8 * ch + 3] * inv);
+                    u.z = pack16<kFmt>(r[8 * ch + 4] * inv, r[8 * ch + 5] * inv);
+                    u.w = pack16<kFmt>(r[8 * ch + 6] * inv, r[8 * ch + 7] * inv);
+                    *reinterpret_cast<uint4 *>(stg + row * 128 + ((ch ^ (row & 7)) << 4)) = u;
+                }
+                fence_proxy_async();
+                mbar_arrive(&stg_full[par]);
+                if (issuer) {
+                    if (!(ok = mbar_spin(&stg_full[par], k & 1, abort_flag, err, kErrWaitPv))) break;
+                    if (q0 < args.seq) tma_store_3d(&tmO, stg, par * 64, q0, bh);
+                    bulk_commit_group();
                 }
             }
+            g0 += n;
         }
     }
+    if (warp >= 2 && (warp - 2) % 4 == 0 && lane == 0) bulk_wait_all();  // output stores complete
     // every thread of both CTAs: the pair's MMAs and TMEM reads are over
     tc_fence_before();
     __syncwarp();
@@ -637,13 +753,36 @@ LaunchFn pair_launch(Context *ctx, const Spec &s) {
     base.causal = s.causal ? 1 : 0;
     base.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)kDim));
     base.err = ctx->err_dev;
-    if (heads_total > 65535 || base.npairs > 65535) throw IrError("attention grid too large for the pair kernel");
-    const dim3 grid(2, heads_total, base.npairs);
+    base.bh_total = heads_total;
+    const long long items = (long long)heads_total * base.npairs;
+    if (items > INT_MAX / 2) throw IrError("attention too large for the pair kernel's work-item index");
+    // persistent: as many CTA pairs as can be resident, each looping over work items
+    int resident = 0;
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * 148);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = Layout::kSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&resident, kernel, &cfg) != cudaSuccess || resident <= 0)
+            throw IrError("cannot size the persistent pair attention grid");
+    }
+    base.clusters = (int)std::min<long long>(items, resident);
+    const dim3 grid(2 * base.clusters);
     const uint64_t bh = heads_total, seq = s.seq;
+    const bool out16 = !std::is_same<TOut, float>::value;
     return [=](cudaStream_t st, void **b) {
-        CUtensorMap mq, mk, mv;
+        CUtensorMap mq, mk, mv, mo;
         if (!make_map(&mq, dt, b[0], bh, seq, 128) || !make_map(&mk, dt, b[1], bh, seq, 64) || !make_map(&mv, dt, b[2], bh, seq, 128))
             return cudaErrorInvalidValue;
+        // 16-bit outputs leave through TMA stores (same element type as the inputs)
+        if (out16 ? !make_map(&mo, dt, b[3], bh, seq, 128) : !make_map(&mo, dt, b[0], bh, seq, 128)) return cudaErrorInvalidValue;
         Args a = base;
         a.out = b[3];
         cudaLaunchConfig_t cfg = {};
@@ -658,7 +797,7 @@ LaunchFn pair_launch(Context *ctx, const Spec &s) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, a);
+        return cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, mo, a);
     };
 }
 

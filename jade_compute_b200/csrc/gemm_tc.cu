@@ -176,19 +176,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (issued[s]) mbar_wait_drain(&full[s], last_phase[s], err);
         }
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------ MMA issuer (whole warp, one elected lane issues)
+        {
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
-                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrWaitAccEmpty)) break;
+            for (int t = blockIdx.x; t < args.num_tiles && !__any_sync(0xffffffffu, *abort_flag); t += gridDim.x) {
+                if (!mbar_wait_warp(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrWaitAccEmpty)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 bool ok = true;
                 for (int kb = 0; kb < args.kblocks; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, err, kErrWaitTmaFull)) { ok = false; break; }
+                    if (!mbar_wait_warp(&full[stage], phase, abort_flag, err, kErrWaitTmaFull)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * kStageBytes);
                     const uint32_t sb = sa + kStageA;
