@@ -14,9 +14,9 @@
 //              so the tensor core works on one tile while the other tile's
 //              softmax runs (ping-pong). P_t(j) is read from TMEM (A operand).
 //   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: one thread per
-//              query row (TMEM lane); pass 1 reads S_t(j) for the row maximum,
-//              pass 2 reads it again, writes P = exp2(S*scale - m) as 16-bit
-//              pairs over the first 64 columns of the same TMEM buffer.
+//              query row (TMEM lane) reads the row of S_t(j) in one round trip and
+//              writes P = exp2(S*scale - m) (attention_softmax.cuh) as 16-bit pairs
+//              over the first 64 columns of the same TMEM buffer.
 // TMEM: S_A | S_B | O_A | O_B (128 columns each). O is rescaled in place only
 // when a row maximum grows by more than 2^8 (until then P <= 256 is exact
 // enough in FP32 accumulation), so steady-state iterations never touch O.
@@ -30,6 +30,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "attention_softmax.cuh"
 #include "common.cuh"
 #include "internal.hpp"
 
@@ -156,6 +157,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         {  // ------------------------------------- MMA issuer (whole warp, one elected lane issues)
             const uint32_t sq0 = smem_u32(smem + L::kQ);
+            // suspending waits: in this kernel the softmax warps sharing the SM
+            // sub-partition are busy while this warp waits, and polling would take
+            // their issue slots (measured slower than try_wait on B200)
+            auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
+                return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, err, code));
+            };
             auto issue_s = [&](int t, int j) {
                 const uint32_t sq = sq0 + t * L::kTile, sk = smem_u32(smem + L::kK + (j & 1) * L::kTile);
 #pragma unroll
@@ -183,14 +190,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; ok && j < nkv_max; ++j) {
                 const bool more = j + 1 < nkv_max;
                 bool k_ready = false;
-                if (!(ok = mbar_wait_warp(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
+                if (!(ok = wait(&v_full[j & 1], (j >> 1) & 1, kErrWaitTmaFull))) break;
                 for (int t = 0; t < 2 && ok; ++t) {
                     if (j >= nkv[t]) continue;
-                    if (!(ok = mbar_wait_warp(&p_full[t], j & 1, abort_flag, err, kErrWaitProb))) break;
+                    if (!(ok = wait(&p_full[t], j & 1, kErrWaitProb))) break;
                     tc_fence_after();
                     issue_pv(t, j);  // reads P_t(j) from TMEM: must precede S_t(j+1)
                     if (j + 1 < nkv[t]) {
-                        if (!k_ready && !(ok = mbar_wait_warp(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, err, kErrWaitTmaFull))) break;
+                        if (!k_ready && !(ok = wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, kErrWaitTmaFull))) break;
                         k_ready = true;
                         tc_fence_after();
                         issue_s(t, j + 1);  // overwrites S_t / P_t
@@ -235,10 +242,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             float mx[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+            for (int e = 0; e < 8; ++e) mx[e] = max3(sv[e], sv[e + 8], sv[e + 16]);
 #pragma unroll
-            for (int i = 8; i < 128; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
-            const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            for (int i = 24; i < 120; i += 16)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx[e] = max3(mx[e], sv[i + e], sv[i + 8 + e]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], sv[120 + e]);
+            const float mraw = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
             const float m_tile = mraw * c;
             // lazy rescale: keep the old maximum unless it grew by more than 2^8
             float m_new = m_used, alpha = 1.0f;
@@ -249,22 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             m_used = m_new;
             // P = exp2(S*c - m) as 16-bit pairs over S's first 64 columns; masked
-            // scores are -inf, so exp2 gives exact zeros.
-            const float neg_m = -m_used;
-            float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-                uint32_t pk[8];
-#pragma unroll
-                for (int i = 0; i < 16; i += 2) {
-                    const float p0 = fast_exp2(fmaf(sv[ch * 16 + i], c, neg_m));
-                    const float p1 = fast_exp2(fmaf(sv[ch * 16 + i + 1], c, neg_m));
-                    ps[(i >> 1) & 3] += p0 + p1;
-                    pk[i / 2] = kFmt == 1 ? pack_bf16(p0, p1) : pack_f16(p0, p1);
-                }
-                tmem_st8(ts + ch * 8, pk);
-            }
-            const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+            // scores are -inf and go through MUFU, which gives exact zeros.
+            const float psum = need_mask ? store_p<kFmt, false, 128>(sv, c, m_used, ts) : store_p<kFmt, kFmt == 1, 128>(sv, c, m_used, ts);
             // O (in TMEM) to the new maxima, after P so the scores' registers are free
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1

@@ -87,6 +87,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         }
     }
 }
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded polling wait (no suspension: the phases waited on here complete within
+// a few hundred cycles, and a suspended waiter can resume much later than that).
+__device__ __forceinline__ bool mbar_spin(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err, int code) {
+    if (mbar_test_wait(bar, parity)) return true;  // usual case: no timer read
+    const uint64_t t0 = globaltimer();
+#pragma unroll 1
+    while (true) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > JADE_WAIT_LIMIT_NS) {
+            if (err) atomicCAS(err, 0, code);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
 // Wait used on exit paths for copies still in flight: ignores the abort flag and
 // only gives up at the time limit.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, int *err) {
