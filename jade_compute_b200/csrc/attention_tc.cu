@@ -66,7 +66,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 template <int D, typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs args) {
     using L = AttnLayout<D>;
     constexpr uint32_t kFmt = std::is_same<TIn, __nv_bfloat16>::value ? 1u : 0u;
     constexpr uint32_t kIdescS = idesc_f32acc(kFmt, kFmt, false, false, kBQ, kBK);
@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *s_full = bars + 9, *p_full = bars + 11, *o_full = bars + 13;  // [tile]
     uint64_t *mma_done = bars + 15;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+    uint64_t *o_staged = bars + 17;  // [tile]: 16-bit O rows written to the tile's Q buffer
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -102,6 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s_full[s], 1); mbar_init(&p_full[s], 128); mbar_init(&o_full[s], 1);
         }
         mbar_init(mma_done, 1);
+        mbar_init(&o_staged[0], 128);
+        mbar_init(&o_staged[1], 128);
         *abort_flag = 0;
         fence_barrier_init();
         fence_proxy_async();
@@ -284,31 +287,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok) {
                 tc_fence_after();
                 const float inv = 1.0f / l_run;
-                TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * D;
+                if constexpr (std::is_same<TOut, float>::value) {
+                    float *o = static_cast<float *>(args.out) + ((size_t)bh * args.seq + q) * D;
 #pragma unroll 1
-                for (int oc = 0; oc < D; oc += 32) {
-                    float r[32];
-                    tmem_ld32f(to + oc, r);
-                    tmem_wait_ld();
-                    if (q < args.seq) {
+                    for (int oc = 0; oc < D; oc += 32) {
+                        float r[32];
+                        tmem_ld32f(to + oc, r);
+                        tmem_wait_ld();
+                        if (q < args.seq)
+#pragma unroll
+                            for (int e = 0; e < 32; e += 4)
+                                *reinterpret_cast<float4 *>(o + oc + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
+                    }
+                } else {
+                    // The tile's Q buffer is free (every S_t MMA completed before the last
+                    // P_t.V did): stage O there in the Q tensor map's layout (64-column
+                    // chunks, 128-byte swizzle) and write it with TMA stores - coalesced,
+                    // clipped at seq, and off the warps' memory pipe.
+                    uint8_t *stg = smem + L::kQ + t * L::kTile;
+#pragma unroll 1
+                    for (int oc = 0; oc < D; oc += 32) {
+                        float r[32];
+                        tmem_ld32f(to + oc, r);
+                        tmem_wait_ld();
+                        uint8_t *rowp = stg + (oc / 64) * L::kChunk + row * 128;
 #pragma unroll
                         for (int e = 0; e < 32; e += 8) {
-                            if constexpr (std::is_same<TOut, float>::value) {
-                                *reinterpret_cast<float4 *>(o + oc + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
-                                *reinterpret_cast<float4 *>(o + oc + e + 4) =
-                                    make_float4(r[e + 4] * inv, r[e + 5] * inv, r[e + 6] * inv, r[e + 7] * inv);
-                            } else {
-                                uint4 u;
-                                if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
-                                    u.x = pack_bf16(r[e] * inv, r[e + 1] * inv); u.y = pack_bf16(r[e + 2] * inv, r[e + 3] * inv);
-                                    u.z = pack_bf16(r[e + 4] * inv, r[e + 5] * inv); u.w = pack_bf16(r[e + 6] * inv, r[e + 7] * inv);
-                                } else {
-                                    u.x = pack_f16(r[e] * inv, r[e + 1] * inv); u.y = pack_f16(r[e + 2] * inv, r[e + 3] * inv);
-                                    u.z = pack_f16(r[e + 4] * inv, r[e + 5] * inv); u.w = pack_f16(r[e + 6] * inv, r[e + 7] * inv);
-                                }
-                                *reinterpret_cast<uint4 *>(o + oc + e) = u;
-                            }
+                            uint4 u;
+                            u.x = pack16<kFmt>(r[e] * inv, r[e + 1] * inv);
+                            u.y = pack16<kFmt>(r[e + 2] * inv, r[e + 3] * inv);
+                            u.z = pack16<kFmt>(r[e + 4] * inv, r[e + 5] * inv);
+                            u.w = pack16<kFmt>(r[e + 6] * inv, r[e + 7] * inv);
+                            const int unit = ((oc % 64) + e) / 8;  // 16-byte unit within the 128-byte row
+                            *reinterpret_cast<uint4 *>(rowp + ((unit ^ (row & 7)) << 4)) = u;
                         }
+                    }
+                    fence_proxy_async();
+                    mbar_arrive(&o_staged[t]);
+                    if (quarter == 2 && lane == 0) {  // one issuer per tile
+                        if (mbar_wait(&o_staged[t], 0, abort_flag, err, kErrWaitPv) && qt[t] * kBQ < args.seq) {
+                            for (int c = 0; c < kDChunks; ++c) tma_store_3d(&tmO, stg + c * L::kChunk, c * 64, qt[t] * kBQ, bh);
+                            bulk_commit_group();
+                        }
+                        bulk_wait_all();  // the stores have read shared memory before the CTA exits
                     }
                 }
             }
@@ -369,9 +390,12 @@ LaunchFn attn_launch(Context *ctx, const Spec &s) {
         CUtensorMap mq, mk, mv;
         if (!make_map3(&mq, dt, b[0], bh, seq, D) || !make_map3(&mk, dt, b[1], bh, seq, D) || !make_map3(&mv, dt, b[2], bh, seq, D))
             return cudaErrorInvalidValue;
+        // 16-bit outputs (same element type as the inputs) leave through TMA stores
+        CUtensorMap mo;
+        if (!make_map3(&mo, dt, std::is_same<TOut, float>::value ? b[0] : b[3], bh, seq, D)) return cudaErrorInvalidValue;
         AttnArgs a = base;
         a.out = b[3];
-        kernel<<<grid, kThreads, L::kSmem, st>>>(mq, mk, mv, a);
+        kernel<<<grid, kThreads, L::kSmem, st>>>(mq, mk, mv, mo, a);
         return cudaGetLastError();
     };
 }
