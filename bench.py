@@ -155,11 +155,20 @@ def cpu_attention_sample(seconds, threads, seed=0):
     return rate / 1e12, f"{count} random causal rows of one head (S={S}, D={D}), FP64 materialized, {dt:.1f} s", threads
 
 
+def host_threads():
+    """Host cores this process may run on. Not the OpenMP default: torchrun sets
+    OMP_NUM_THREADS=1 in every rank, and the CPU baselines pass this count
+    explicitly to the oracle."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def run_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
         return 0  # under torchrun only rank 0 times the host implementation
-    from oracle import oracle as O
-    threads = O.max_threads()
+    threads = host_threads()
     per_step = max(1.0, min(10.0, 60.0 / max(args.steps + args.warmup, 1)))
     for _ in range(args.warmup):
         cpu_attention_sample(per_step / 4, threads, seed=1)
@@ -426,7 +435,7 @@ def run_ours(args):
         cpu = None
         if rank == 0 and not args.no_cpu:
             from oracle import oracle as O
-            thr = O.max_threads()
+            thr = host_threads()
             rate, desc, cores = cpu_attention_sample(args.cpu_seconds, thr)
             cpu = {"value": rate, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": desc}
         achieved = per_gpu

@@ -54,6 +54,7 @@ struct AttnLayout {
 struct AttnArgs {
     void *out;
     int seq, nq_tiles, npairs, nkv_tiles, causal;
+    int bh_total, group_heads;  // block order: heads in L2-sized groups, heaviest pairs first
     float scale_log2;
     int *err;
 };
@@ -85,8 +86,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.x;
-    const int pair = args.npairs - 1 - (int)blockIdx.y;  // heaviest causal pairs first
+    // Block b covers head group g (group_heads heads whose K/V fit in L2 together, so
+    // the blocks resident at one time share cached K/V) and, inside it, the heaviest
+    // causal q-tile pairs first.
+    int bh, pair;
+    {
+        const int b = blockIdx.x, per_group = args.group_heads * args.npairs, g = b / per_group;
+        const int h0 = g * args.group_heads, hg = min(args.group_heads, args.bh_total - h0), i = b - g * per_group;
+        bh = h0 + i % hg;
+        pair = args.npairs - 1 - i / hg;
+    }
     int qt[2], nkv[2];
     for (int t = 0; t < 2; ++t) {
         qt[t] = 2 * pair + t;
@@ -384,7 +393,10 @@ LaunchFn attn_launch(Context *ctx, const Spec &s) {
     base.causal = s.causal ? 1 : 0;
     base.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
     base.err = ctx->err_dev;
-    const dim3 grid(heads_total, base.npairs);
+    base.bh_total = heads_total;
+    base.group_heads = (int)std::max<long long>(1, std::min<long long>(heads_total, (64ll << 20) / (4ll * (long long)s.seq * D)));
+    if ((long long)heads_total * base.npairs > INT_MAX) throw IrError("attention too large for one launch");
+    const dim3 grid(heads_total * base.npairs);
     const uint64_t bh = heads_total, seq = s.seq;
     return [=](cudaStream_t st, void **b) {
         CUtensorMap mq, mk, mv;

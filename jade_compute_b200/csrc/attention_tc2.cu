@@ -57,6 +57,7 @@ constexpr int kStages = 3;     // K and V ring depth (V loads trail K by one ste
 // other the odd ones, each thread a whole row (128 scores) of its steps
 constexpr int kCols = kKeys;
 constexpr int kThreads = 10 * 32;
+constexpr int kMaxItems = 512;   // work items per CTA pair (the host checks the bound)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct Layout {
@@ -73,14 +74,17 @@ struct Layout {
     // floats: running-maximum tokens [2][128]; per work item (double-buffered)
     // final maxima [2][2][128] and row sums [2][2][128]
     static constexpr uint32_t kRed = kBar + 512;
-    static constexpr uint32_t kSmem = kRed + (256 + 512 + 512) * 4 + 1024;
+    // this pair's work items (computed once at start; every role reads them here)
+    static constexpr uint32_t kItems = kRed + (256 + 512 + 512) * 4;
+    static constexpr uint32_t kSmem = kItems + kMaxItems * 4 + 1024;
 };
 
 struct Args {
     void *out;
     int seq, nq_tiles, npairs, nkv_tiles, causal;
-    int bh_total;  // batch * heads
-    int clusters;  // CTA pairs launched; pair c takes work items c, c + clusters, ...
+    int bh_total;     // batch * heads
+    int clusters;     // CTA pairs launched (persistent)
+    int group_heads;  // heads per L2 group of the work order
     float scale_log2;
     int *err;
 };
@@ -178,7 +182,9 @@ __device__ __forceinline__ float load_row_max(float (&sv)[kCols], uint32_t ts, i
     return max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * c;
 }
 
-template <typename TIn, typename TOut>
+// kGrouped: heads in L2-sized groups (the work items' K/V exceed the L2 budget);
+// otherwise the single heavy-first order, computed inline.
+template <typename TIn, typename TOut, bool kGrouped>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const Args args) {
@@ -219,18 +225,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int p = item_pair(it);
         return args.causal ? min(2 * p + 2, args.nkv_tiles) : args.nkv_tiles;
     };
-    // this pair's k-th work item: boustrophedon over the heavy-first order (round k
-    // runs the pairs forward for even k, backward for odd k), which balances the
-    // causal triangle to within a few percent; -1 when the pair has no k-th item
+    // This pair's k-th work item, -1 past the last. Heads are taken in groups of
+    // group_heads whose K/V fit in L2 together, so concurrently running items share
+    // cached K/V; within a group the items go heaviest pair index first, dealt out
+    // boustrophedon (round r forward for even r, backward for odd r), which
+    // balances the causal triangle to within a few percent. Items are numbered
+    // it = pair_order * bh_total + head.
+    auto item_order = [&](int k) {
+        const int C = args.clusters;
+        for (int h0 = 0; h0 < args.bh_total; h0 += args.group_heads) {
+            const int hg = min(args.group_heads, args.bh_total - h0), G = hg * args.npairs;
+            const int full = G / C, rem = G % C, slot_last = (full & 1) ? C - 1 - cluster : cluster;
+            const int mine = full + (rem > 0 && slot_last < rem ? 1 : 0);
+            if (k < mine) {
+                const int i = k * C + ((k & 1) ? C - 1 - cluster : cluster);
+                return (i / hg) * args.bh_total + h0 + i % hg;
+            }
+            k -= mine;
+        }
+        return -1;
+    };
+    int *items = reinterpret_cast<int *>(smem + L::kItems);  // this pair's items, -1 terminated (grouped order)
     auto item_of = [&](int k) {
-        const int it = k * args.clusters + ((k & 1) ? args.clusters - 1 - cluster : cluster);
-        return it < total_items ? it : -1;
+        if constexpr (kGrouped) {
+            return items[k];
+        } else {
+            const int it = k * args.clusters + ((k & 1) ? args.clusters - 1 - cluster : cluster);
+            return it < total_items ? it : -1;
+        }
     };
     int total_steps = 0;  // key steps over all of this pair's work items
-    for (int k = 0, it; (it = item_of(k)) >= 0; ++k) total_steps += item_steps(it);
+    if constexpr (!kGrouped)
+        for (int k = 0, it; (it = item_of(k)) >= 0; ++k) total_steps += item_steps(it);
     int *err = args.err;
 
     if (threadIdx.x == 0) {
+        if constexpr (kGrouped) {
+            int k = 0;
+            for (int it; k < kMaxItems - 1 && (it = item_order(k)) >= 0; ++k) items[k] = it;
+            items[k] = -1;
+        }
         for (int b = 0; b < 2; ++b) { mbar_init(&q_full[b], 1); mbar_init(&q_empty[b], 1); }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
@@ -259,6 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     cluster_sync();  // barriers and TMEM of both CTAs exist before any cross-CTA use
     tc_fence_after();
+    if constexpr (kGrouped)  // the list in shared memory is complete now
+        for (int k = 0, it; (it = item_of(k)) >= 0; ++k) total_steps += item_steps(it);
     const uint32_t tmem = *tmem_slot;
     const uint32_t tmem_o = tmem + 384;
 
@@ -599,7 +635,11 @@ bool make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_
 
 template <typename TIn, typename TOut>
 LaunchFn pair_launch(Context *ctx, const Spec &s) {
-    auto kernel = attention_pair_kernel<TIn, TOut>;
+    const long long heads_all = (long long)s.batch * s.heads;
+    // heads whose K and V (2 x seq x 128 x 2 bytes each) fit in about 64 MB of the 126 MB L2
+    const int group_heads = (int)std::max<long long>(1, std::min<long long>(heads_all, (64ll << 20) / (4ll * (long long)s.seq * kDim)));
+    const bool grouped = group_heads < heads_all;
+    auto kernel = grouped ? attention_pair_kernel<TIn, TOut, true> : attention_pair_kernel<TIn, TOut, false>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Layout::kSmem) != cudaSuccess)
         throw IrError("cannot reserve shared memory for the tcgen05 pair attention");
     const CUtensorMapDataType dt = std::is_same<TIn, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -633,6 +673,13 @@ LaunchFn pair_launch(Context *ctx, const Spec &s) {
             throw IrError("cannot size the persistent pair attention grid");
     }
     base.clusters = (int)std::min<long long>(items, resident);
+    base.group_heads = group_heads;
+    if (grouped) {  // items per pair: at most ceil(group items / pairs) per head group
+        long long bound = 0;
+        for (long long h0 = 0; h0 < heads_total; h0 += base.group_heads)
+            bound += (std::min<long long>(base.group_heads, heads_total - h0) * base.npairs + base.clusters - 1) / base.clusters;
+        if (bound > kMaxItems - 1) throw IrError("attention has too many work items per SM pair for the pair kernel");
+    }
     const dim3 grid(2 * base.clusters);
     const uint64_t bh = heads_total, seq = s.seq;
     const bool out16 = !std::is_same<TOut, float>::value;

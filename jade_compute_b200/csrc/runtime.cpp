@@ -382,7 +382,11 @@ extern "C" int jr_compile(void *handle, const char *spec_json, jr_kernel **out, 
                     // CTA-pair kernel: faster once each pair streams enough key tiles to
                     // amortise its per-tile set-up (measured on B200; the two-tile
                     // kernel below wins for shorter causal rows)
-                    k->run = jade::make_attention_pair(ctx, s, k->impl);
+                    try {
+                        k->run = jade::make_attention_pair(ctx, s, k->impl);
+                    } catch (const jade::IrError &) {  // more work items than the pair kernel's list holds
+                        k->run = jade::make_attention_tc(ctx, s, k->impl);
+                    }
                     k->path = "tcgen05";
                 } else {
                     k->run = jade::make_attention_tc(ctx, s, k->impl);
