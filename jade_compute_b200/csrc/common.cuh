@@ -199,6 +199,46 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// Groups of kind::f16 MMAs into one accumulator, issued with a single election
+// (whole warp): D (+)= A_0 B_0, then D += A_i B_i for i >= 1. `accumulate`
+// applies to the first MMA only. The fewer instructions per MMA keep the issue
+// ahead of the tensor core when the issuing warp shares its sub-partition with
+// busy warps (a 128x128x16 MMA executes in 64 cycles).
+#define JADE_UMMA_HEAD "{\n\t.reg .pred p, q, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %2, 0;\n\tsetp.ne.b32 q, 1, 0;\n\t"
+#define JADE_UMMA_SS(a, b, pr) "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %" #a ", %" #b ", %1, " #pr ";\n\t"
+#define JADE_UMMA_TS(a, b, pr) "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%" #a "], %" #b ", %1, " #pr ";\n\t"
+// N = 4 or 8: A and B from shared-memory descriptors
+template <int N>
+__device__ __forceinline__ void umma_ss_group(uint32_t d_tmem, const uint64_t (&a)[N], const uint64_t (&b)[N], uint32_t idesc,
+                                              uint32_t accumulate) {
+    static_assert(N == 4 || N == 8, "groups of 4 or 8 MMAs");
+    if constexpr (N == 4) {
+        asm volatile(JADE_UMMA_HEAD JADE_UMMA_SS(3, 7, p) JADE_UMMA_SS(4, 8, q) JADE_UMMA_SS(5, 9, q) JADE_UMMA_SS(6, 10, q) "}" ::"r"(d_tmem),
+                     "r"(idesc), "r"(accumulate), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3])
+                     : "memory");
+    } else {
+        asm volatile(JADE_UMMA_HEAD JADE_UMMA_SS(3, 11, p) JADE_UMMA_SS(4, 12, q) JADE_UMMA_SS(5, 13, q) JADE_UMMA_SS(6, 14, q)
+                         JADE_UMMA_SS(7, 15, q) JADE_UMMA_SS(8, 16, q) JADE_UMMA_SS(9, 17, q) JADE_UMMA_SS(10, 18, q) "}" ::"r"(d_tmem),
+                     "r"(idesc), "r"(accumulate), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]),
+                     "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7])
+                     : "memory");
+    }
+}
+// 8 MMAs with A read from TMEM (a_tmem + 8 i: 16 columns of 16-bit pairs each) and
+// B from shared-memory descriptors
+__device__ __forceinline__ void umma_ts_group8(uint32_t d_tmem, uint32_t a_tmem, const uint64_t (&b)[8], uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(JADE_UMMA_HEAD JADE_UMMA_TS(3, 11, p) JADE_UMMA_TS(4, 12, q) JADE_UMMA_TS(5, 13, q) JADE_UMMA_TS(6, 14, q)
+                     JADE_UMMA_TS(7, 15, q) JADE_UMMA_TS(8, 16, q) JADE_UMMA_TS(9, 17, q) JADE_UMMA_TS(10, 18, q) "}" ::"r"(d_tmem),
+                 "r"(idesc), "r"(accumulate), "r"(a_tmem), "r"(a_tmem + 8), "r"(a_tmem + 16), "r"(a_tmem + 24), "r"(a_tmem + 32),
+                 "r"(a_tmem + 40), "r"(a_tmem + 48), "r"(a_tmem + 56), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]),
+                 "l"(b[5]), "l"(b[6]), "l"(b[7])
+                 : "memory");
+}
+#undef JADE_UMMA_HEAD
+#undef JADE_UMMA_SS
+#undef JADE_UMMA_TS
+
 // Arrive once on `bar` when every tcgen05 operation issued so far by the elected
 // lane completes (whole warp; the same lane is elected each time in a converged warp).
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {

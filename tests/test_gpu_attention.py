@@ -82,6 +82,22 @@ def test_attention_baseline_config2_sampled(rt, causal):
     check(got, qf, kf, vf, S, D, causal, (bh, rows), True)
 
 
+@pytest.mark.parametrize("B,H,S,D,causal,out_dtype", [
+    (2, 80, 2048, 128, True, None),    # 1280 items in 3 head groups (K/V of 64 heads per L2 group)
+    (1, 150, 1100, 128, True, "fp32"),  # 9 q tiles: the heaviest item of every head has one tile
+    (3, 50, 1000, 64, False, None),     # head dim 64, 600 equal items
+    (1, 300, 4200, 64, True, None),     # 300 heads in 5 groups, tail tile of 104 keys
+], ids=["groups", "odd-tiles-fp32", "d64-full", "groups-d64-tail"])
+def test_attention_persistent_items(rt, B, H, S, D, causal, out_dtype):
+    # the two-tile kernel is persistent: each CTA walks several (head, q-tile pair)
+    # items, reusing its Q buffers, TMEM and O staging across them
+    got, qf, kf, vf = run_attention(rt, B, H, S, D, causal, out_dtype=out_dtype, seed=S + H)
+    rng = np.random.default_rng(S)
+    bh = np.concatenate([[0, B * H - 1, B * H // 2], rng.integers(0, B * H, 93)])
+    rows = np.concatenate([[0, S - 1, 127, 128 % S], rng.integers(0, S, 92)])
+    check(got, qf, kf, vf, S, D, causal, (bh, rows), out_dtype is None)
+
+
 def test_attention_uniform_rows_kat(rt):
     # metal_lab.rs:471-484 restated: Q = K = 0 gives uniform weights, so each
     # output row is the mean of the visible V rows (exact in any precision order
