@@ -79,8 +79,8 @@ __device__ __forceinline__ void reg_fence(float (&v)[N]) {
 }
 // P = exp2(s * c - m) for a row of scores, written as 16-bit pairs to TMEM
 // columns [ts, ts + kCols/2) eight at a time; returns the row sum.
-// kPoly: evaluate kPolyPairs of every 8 pairs with the FMA-pipe polynomial.
-template <uint32_t kFmt, bool kPoly, int kCols>
+// kPoly: evaluate kPolyN of every 8 pairs with the FMA-pipe polynomial.
+template <uint32_t kFmt, bool kPoly, int kCols, int kPolyN = kPolyPairs>
 __device__ __forceinline__ float store_p(const float (&sv)[kCols], float c, float m, uint32_t ts) {
     const uint64_t c2 = pack2f(c, c), nm2 = pack2f(-m, -m);
     uint64_t acc[2] = {pack2f(0.0f, 0.0f), pack2f(0.0f, 0.0f)};
@@ -91,7 +91,7 @@ __device__ __forceinline__ float store_p(const float (&sv)[kCols], float c, floa
         for (int i = 0; i < 8; ++i) {
             const uint64_t xv = fma2(pack2f(sv[16 * g + 2 * i], sv[16 * g + 2 * i + 1]), c2, nm2);
             uint64_t p;
-            if (kPoly && i < kPolyPairs) {
+            if (kPoly && i < kPolyN) {
                 p = poly_exp2_pair(xv);
             } else {
                 float x0, x1;
