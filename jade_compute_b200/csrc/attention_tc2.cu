@@ -132,22 +132,33 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 // The issuing helpers below are executed by a whole converged warp and issue
 // from one elected lane: issuing from a single divergent thread starves the
 // tensor core when the SM sub-partition is shared with busy softmax warps.
-// D[tmem] (+)= A[smem] * B[smem], M=256 over the CTA pair.
-__device__ __forceinline__ void umma_pair_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
+// Eight M=256 MMAs into one accumulator under a single election (whole warp):
+// D (+)= A_0 B_0, then D += A_i B_i. `accumulate` applies to the first only; fewer
+// instructions per MMA keep the issue ahead of the tensor core (each executes in 64
+// cycles per SM) when this warp shares its sub-partition with softmax warps.
+#define JADE_PAIR_HEAD "{\n\t.reg .pred p, q, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %2, 0;\n\tsetp.ne.b32 q, 1, 0;\n\t"
+#define JADE_PAIR_SS(a, b, pr) "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %" #a ", %" #b ", %1, " #pr ";\n\t"
+#define JADE_PAIR_TS(a, b, pr) "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%" #a "], %" #b ", %1, " #pr ";\n\t"
+__device__ __forceinline__ void umma_pair_ss8(uint32_t d_tmem, const uint64_t (&a)[8], const uint64_t (&b)[8], uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(JADE_PAIR_HEAD JADE_PAIR_SS(3, 11, p) JADE_PAIR_SS(4, 12, q) JADE_PAIR_SS(5, 13, q) JADE_PAIR_SS(6, 14, q)
+                     JADE_PAIR_SS(7, 15, q) JADE_PAIR_SS(8, 16, q) JADE_PAIR_SS(9, 17, q) JADE_PAIR_SS(10, 18, q) "}" ::"r"(d_tmem),
+                 "r"(idesc), "r"(accumulate), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]),
+                 "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7])
+                 : "memory");
 }
-// D[tmem] (+)= A[tmem] * B[smem], M=256 over the CTA pair.
-__device__ __forceinline__ void umma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
+// A from TMEM at a_tmem + 8 i (16-bit pairs), B from shared-memory descriptors
+__device__ __forceinline__ void umma_pair_ts8(uint32_t d_tmem, uint32_t a_tmem, const uint64_t (&b)[8], uint32_t idesc, uint32_t accumulate) {
+    asm volatile(JADE_PAIR_HEAD JADE_PAIR_TS(3, 11, p) JADE_PAIR_TS(4, 12, q) JADE_PAIR_TS(5, 13, q) JADE_PAIR_TS(6, 14, q)
+                     JADE_PAIR_TS(7, 15, q) JADE_PAIR_TS(8, 16, q) JADE_PAIR_TS(9, 17, q) JADE_PAIR_TS(10, 18, q) "}" ::"r"(d_tmem),
+                 "r"(idesc), "r"(accumulate), "r"(a_tmem), "r"(a_tmem + 8), "r"(a_tmem + 16), "r"(a_tmem + 24), "r"(a_tmem + 32),
+                 "r"(a_tmem + 40), "r"(a_tmem + 48), "r"(a_tmem + 56), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]),
+                 "l"(b[5]), "l"(b[6]), "l"(b[7])
+                 : "memory");
 }
+#undef JADE_PAIR_HEAD
+#undef JADE_PAIR_SS
+#undef JADE_PAIR_TS
 // One arrival on the mbarrier at `bar_cluster_addr` (either CTA) once every
 // tcgen05 operation issued so far by the elected thread has completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
@@ -351,6 +362,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             auto wait = [&](uint64_t *bar, uint32_t parity, int code) {
                 return __all_sync(0xffffffffu, mbar_spin(bar, parity, abort_flag, err, code));
             };
+            // Descriptors are built once and advanced by the 16-byte address units of each
+            // operand (the start address is the low 14 bits; shared memory stays below
+            // 256 KB, so the additions never carry out of the field).
+            const uint64_t dq0 = sdesc_sw128(smem_u32(smem + L::kQ), 16, 1024);
+            const uint64_t dk0 = sdesc_sw128(smem_u32(smem + L::kK), 16, 1024);
+            const uint64_t dv0 = sdesc_sw128(smem_u32(smem + L::kV), 16384, 1024);
             // S issue cursor: work item (index it, sequence number k, n steps), local step j
             int s_k = 0, s_j = 0, s_n = item_of(0) >= 0 ? item_steps(item_of(0)) : 0;
             auto issue_s = [&](int gs, bool wait_inputs) {  // S(gs) = Q K^T into buffer gs % 3
@@ -360,12 +377,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!wait(&k_full[st], (gs / kStages) & 1, kErrWaitTmaFull)) return false;
                 }
                 tc_fence_after();
-                const uint32_t sq = smem_u32(smem + L::kQ + qb * L::kQBuf);
-                const uint32_t sk = smem_u32(smem + L::kK + st * L::kKStage);
+                const uint64_t dq = dq0 + ((qb * L::kQBuf) >> 4), dk = dk0 + ((st * L::kKStage) >> 4);
+                uint64_t a[kDim / 16], b[kDim / 16];
 #pragma unroll
-                for (int k = 0; k < kDim / 16; ++k)
-                    umma_pair_ss(tmem + (gs % 3) * 128, sdesc_sw128(sq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
-                                 sdesc_sw128(sk + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024), kIdescS, k != 0);
+                for (int k = 0; k < kDim / 16; ++k) {
+                    a[k] = dq + (((k >> 2) * 16384 + (k & 3) * 32) >> 4);
+                    b[k] = dk + (((k >> 2) * 8192 + (k & 3) * 32) >> 4);
+                }
+                umma_pair_ss8(tmem + (gs % 3) * 128, a, b, kIdescS, 0);
                 commit_both(&s_full[gs % 3]);
                 commit_both(&k_empty[st]);
                 if (s_j == s_n - 1) commit_both(&q_empty[qb]);  // the item's last S: its Q buffer is free
@@ -400,11 +419,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (first && !(ok = wait(o_free, (p_k - 1) & 1, kErrWaitPv))) break;
                 }
                 tc_fence_after();
-                const uint32_t sv = smem_u32(smem + L::kV + st * L::kVStage);
-                const uint32_t sp = tmem + (g % 3) * 128;
+                const uint64_t dv = dv0 + ((st * L::kVStage) >> 4);
+                uint64_t b[kKeys / 16];
 #pragma unroll
-                for (int k = 0; k < kKeys / 16; ++k)  // keys 16k..16k+15: P columns 8k..8k+7
-                    umma_pair_ts(tmem_o, sp + k * 8, sdesc_sw128(sv + k * 2048, 16384, 1024), kIdescO, (p_j | k) != 0);
+                for (int k = 0; k < kKeys / 16; ++k) b[k] = dv + ((k * 2048) >> 4);  // keys 16k..16k+15: P columns 8k..8k+7
+                umma_pair_ts8(tmem_o, tmem + (g % 3) * 128, b, kIdescO, p_j != 0);
                 commit_both(&v_empty[st]);
                 if (g == total_steps - 3) commit_both(&o_tail[0]);
                 if (g == total_steps - 2) commit_both(&o_tail[1]);

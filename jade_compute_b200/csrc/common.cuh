@@ -87,6 +87,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         }
     }
 }
+// try_wait that lets the thread sleep up to `ns` nanoseconds (it wakes when the
+// phase completes): for waits that may last many microseconds, so that the waiting
+// warp does not loop on its sub-partition beside busy warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait built on mbar_try_wait_sleep (same contract as mbar_wait).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err, int code,
+                                                uint32_t ns = 20000) {
+    if (mbar_try_wait_sleep(bar, parity, ns)) return true;
+    const uint64_t t0 = globaltimer();
+#pragma unroll 1
+    while (true) {
+        if (mbar_try_wait_sleep(bar, parity, ns)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > JADE_WAIT_LIMIT_NS) {
+            if (err) atomicCAS(err, 0, code);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
 __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -166,6 +196,11 @@ __device__ __forceinline__ void tmem_relinquish() {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
+// Warp-group register reallocation (all four warps of the group execute it).
+template <int N>
+__device__ __forceinline__ void reg_alloc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void reg_dealloc() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
