@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 #include <functional>
 #include <map>
@@ -64,6 +65,19 @@ bool gemm_tc_supports(const Spec &s, std::string &why);
 LaunchFn make_attention_simt(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_attention_tc(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_attention_pair(Context *ctx, const Spec &s, std::string &impl);  // dim 128, CTA pairs
+// Which 16-bit attention kernel to run, from measurements on B200. Both deal
+// (head, 256-query) work items to persistent workers: the two-tile kernel to one
+// CTA per SM, the pair kernel to one CTA pair per two SMs. The two-tile kernel has
+// the faster key step (about 9% at long rows) and wins causal attention at every
+// length; the pair kernel wins non-causal shapes whose item count leaves the last
+// round of the two-tile kernel mostly empty (e.g. 512 items on 148 SMs: 3.46 of 4
+// rounds), as it spreads the same items over half as many workers.
+inline bool attention_prefers_pair(const Spec &s, int sm_count) {
+    if (s.causal || s.dim != 128 || s.seq < 2048 || sm_count < 2) return false;
+    const double items = (double)s.batch * s.heads * (double)((s.seq + 255) / 256);
+    auto efficiency = [&](double workers) { return items / (std::ceil(items / workers) * workers); };
+    return efficiency(sm_count) < 0.92 * efficiency(sm_count / 2);
+}
 LaunchFn make_elementwise_rtc(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl);  // fill, l2_flush
 LaunchFn make_cublas_gemm(Context *ctx, const Spec &s, std::string &impl);

@@ -16,6 +16,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <thread>
@@ -102,6 +103,20 @@ void *driver_entry(const char *name) {
 }  // namespace jade
 
 // ============================================================== ABI 1
+namespace {
+// 16-bit attention kernel choice: JADE_ATTENTION_KERNEL=pair or two_tile forces one
+// (read when a kernel is compiled); otherwise the measured rule of
+// attention_prefers_pair decides.
+bool attention_use_pair(const jade::Spec &s, int sm_count) {
+    const char *force = std::getenv("JADE_ATTENTION_KERNEL");
+    if (!force || !*force) return jade::attention_prefers_pair(s, sm_count);
+    if (std::strcmp(force, "two_tile") == 0) return false;
+    if (std::strcmp(force, "pair") != 0) throw jade::IrError("JADE_ATTENTION_KERNEL must be pair or two_tile");
+    if (s.dim != 128) throw jade::IrError("the pair attention kernel needs head dim 128");
+    return true;
+}
+}  // namespace
+
 extern "C" uint32_t jr_version(void) { return 1; }
 
 extern "C" int jr_create(int device, void **out, char *err, size_t cap) {
@@ -378,10 +393,7 @@ extern "C" int jr_compile(void *handle, const char *spec_json, jr_kernel **out, 
                 if (s.dtype == jade::DType::F32) {
                     k->run = jade::make_attention_simt(ctx, s, k->impl);
                     k->path = "simt";
-                } else if (s.op == Op::AttentionOnline && s.dim == 128 && (s.causal ? s.seq >= 6144 : s.seq >= 2048)) {
-                    // CTA-pair kernel: faster once each pair streams enough key tiles to
-                    // amortise its per-tile set-up (measured on B200; the two-tile
-                    // kernel below wins for shorter causal rows)
+                } else if (s.op == Op::AttentionOnline && attention_use_pair(s, ctx->sm_count)) {
                     try {
                         k->run = jade::make_attention_pair(ctx, s, k->impl);
                     } catch (const jade::IrError &) {  // more work items than the pair kernel's list holds

@@ -115,18 +115,48 @@ def test_attention_uniform_rows_kat(rt):
 
 
 # ---------------------------------------------------------------- CTA-pair kernel
-# Head dim 128 with long key ranges (non-causal S >= 2048, causal S >= 6144) runs
-# on the cta_group::2 kernel (attention_tc2.cu): S triple-buffered in TMEM, two
-# softmax warps per lane quarter on alternating key steps, speculative maxima.
+# The cta_group::2 kernel (attention_tc2.cu: S triple-buffered in TMEM, two softmax
+# warps per lane quarter on alternating key steps, speculative maxima) runs
+# non-causal head-dim-128 shapes whose work items fill its 74 CTA pairs better than
+# the two-tile kernel's 148 SMs; JADE_ATTENTION_KERNEL=pair forces it, which these
+# tests do so that its causal path stays covered too.
 
 def pair_impl(kern):
     return "pair" in kern.info.get("impl", "")
 
 
+@pytest.fixture
+def pair_kernel(monkeypatch):
+    monkeypatch.setenv("JADE_ATTENTION_KERNEL", "pair")
+
+
+def kernel_impl(rt, B, H, S, causal, D=128):
+    return rt.compile({"op": "attention_online", "heads": H, "seq": S, "dim": D, "causal": causal, "dtype": "bf16",
+                       "batch": B}).info["impl"]
+
+
+def test_attention_kernel_choice(rt, monkeypatch):
+    # measured rule: causal always two-tile; non-causal 512 items (3.46 rounds of the
+    # two-tile kernel's 148 SMs) go to the pair kernel, 2048 items do not
+    assert "pair" not in kernel_impl(rt, 4, 16, 2048, True)
+    assert "pair" in kernel_impl(rt, 4, 16, 2048, False)
+    assert "pair" not in kernel_impl(rt, 8, 16, 4096, False)
+    assert "pair" not in kernel_impl(rt, 16, 16, 1024, False)
+    monkeypatch.setenv("JADE_ATTENTION_KERNEL", "two_tile")
+    assert "pair" not in kernel_impl(rt, 4, 16, 2048, False)
+    monkeypatch.setenv("JADE_ATTENTION_KERNEL", "pair")
+    assert "pair" in kernel_impl(rt, 4, 16, 2048, True)
+    with pytest.raises(jc.JadeError, match="head dim 128"):
+        kernel_impl(rt, 1, 1, 256, False, D=64)
+    monkeypatch.setenv("JADE_ATTENTION_KERNEL", "fastest")
+    with pytest.raises(jc.JadeError, match="pair or two_tile"):
+        kernel_impl(rt, 1, 1, 256, False)
+
+
 @pytest.mark.parametrize("B,H,S,causal", [(1, 2, 2048, False), (1, 1, 2100, False), (2, 1, 2304, False),
                                           (1, 1, 6144, True), (1, 1, 6200, True)],
                          ids=["full2048", "full2100tail", "full2304", "causal6144", "causal6200tail"])
-def test_attention_pair_kernel(rt, B, H, S, causal):
+def test_attention_pair_kernel(rt, pair_kernel, B, H, S, causal):
     D = 128
     got, qf, kf, vf = run_attention(rt, B, H, S, D, causal, seed=S + 7)
     kern = rt.compile({"op": "attention_online", "heads": H, "seq": S, "dim": D, "causal": causal, "dtype": "bf16", "batch": B})
@@ -141,14 +171,14 @@ def test_attention_pair_kernel(rt, B, H, S, causal):
 
 
 @pytest.mark.parametrize("dtype,out_dtype", [("fp16", None), ("bf16", "fp32")])
-def test_attention_pair_kernel_dtypes(rt, dtype, out_dtype):
+def test_attention_pair_kernel_dtypes(rt, pair_kernel, dtype, out_dtype):
     B, H, S, D = 1, 1, 2048, 128
     got, qf, kf, vf = run_attention(rt, B, H, S, D, False, dtype, out_dtype, seed=5)
     rows = np.arange(0, S, 3)
     check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), (out_dtype or dtype) != "fp32")
 
 
-def test_attention_pair_kernel_rescales(rt):
+def test_attention_pair_kernel_rescales(rt, pair_kernel):
     # scores that grow along the keys force the running maximum up by far more
     # than 2^8 at every key step: the speculative P is redone and O rescaled each step
     B, H, S, D = 1, 1, 2048, 128
@@ -169,7 +199,7 @@ def test_attention_pair_kernel_rescales(rt):
     check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), True)
 
 
-def test_attention_pair_kernel_uniform_kat(rt):
+def test_attention_pair_kernel_uniform_kat(rt, pair_kernel):
     # Q = K = 0: every non-causal output row is the mean of all V rows
     B, H, S, D = 1, 1, 2048, 128
     n = S * D
