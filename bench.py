@@ -7,7 +7,9 @@ Contract (one JSON line on rank 0):
              HBM, L2 flushed (256 MiB write) between steps; max over ranks.
   e2e        the same metric through the public API with host buffers: each step
              copies Q, K, V from pinned host memory, runs attention and copies O
-             back, all as jobs of one ordered batch, event-timed on the stream.
+             back, all as jobs of one batch with the transfers on their own
+             streams ordered by data dependencies (JR_EXEC_STREAMS: a step's O
+             read-back overlaps the next step's uploads), event-timed.
   roofline   tensor-bound: algorithmic FLOPs per launch / mean launch time vs the
              measured dense BF16 peak; traffic from the committed ncu summary.
   cpu_baseline  the FP64 oracle (the reference's CPU attention restated,
@@ -416,10 +418,12 @@ def run_ours(args):
         h2d = rt.compile({"op": "copy", "bytes": 2 * n, "direction": "h2d"})
         d2h = rt.compile({"op": "copy", "bytes": 2 * n, "direction": "d2h"})
         e2e_jobs = [(h2d, [hq, q]), (h2d, [hk, k]), (h2d, [hv, v]), (attn, [q, k, v, o]), (d2h, [o, ho])]
-        rt.execute(e2e_jobs, repeats=2)
+        # transfers on their own streams (JR_EXEC_STREAMS), ordered by the data
+        # dependencies: a step's O read-back overlaps the next step's uploads
+        rt.execute(e2e_jobs, repeats=2, streams=True)
         e2e_steps = max(3, min(args.steps, 50))
         barrier(dist)
-        te = rt.execute(e2e_jobs, repeats=e2e_steps, per_job=True)
+        te = rt.execute(e2e_jobs, repeats=e2e_steps, per_job=True, streams=True)
         e2e_ms = reduce_max(dist, te.gpu_ms) / e2e_steps
         e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
         components = []

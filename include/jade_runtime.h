@@ -109,6 +109,14 @@ typedef struct jr_dispatch {
 } jr_dispatch;
 
 #define JR_EXEC_GRAPH 1u /* capture one pass as a CUDA graph, replay it `repeats` times */
+/* Dependency-scheduled streams (not with JR_EXEC_GRAPH): host-to-device copy jobs
+ * run on a transfer-in stream, device-to-host copy jobs on a transfer-out stream,
+ * every other job on the context stream; each job first waits for the jobs it
+ * conflicts with on its bindings (read after write, write after write, write after
+ * read), so results equal in-order execution while transfers overlap compute and
+ * each other (e.g. one repeat's result read-back with the next repeat's uploads).
+ * No counterpart in the reference (its execute is strictly in order). */
+#define JR_EXEC_STREAMS 2u
 
 /* Validates every job (context ownership, registered buffers, exact byte sizes,
  * output aliasing - corex.rs:557-569, ir.rs:340-367) before any work is

@@ -12,7 +12,9 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <chrono>
+#include <map>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -61,6 +63,9 @@ void destroy(Context *ctx) {
         else cudaFree(reinterpret_cast<void *>(a.first));
     }
     for (auto e : ctx->job_events) cudaEventDestroy(e);
+    for (auto e : ctx->dep_events) cudaEventDestroy(e);
+    if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+    if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->start) cudaEventDestroy(ctx->start);
     if (ctx->stop) cudaEventDestroy(ctx->stop);
@@ -517,8 +522,10 @@ extern "C" int jr_execute2(void *handle, const jr_dispatch *jobs, size_t job_cou
     clear(err, cap);
     if (gpu_ms) *gpu_ms = 0;
     if (!jobs || !job_count || !repeats || !gpu_ms) return fail(JR_EINVAL, err, cap, "empty dispatch sequence or missing timing output");
-    const bool graph = flags & JR_EXEC_GRAPH;
+    const bool graph = flags & JR_EXEC_GRAPH, streams = flags & JR_EXEC_STREAMS;
+    if (flags & ~(JR_EXEC_GRAPH | JR_EXEC_STREAMS)) return fail(JR_EINVAL, err, cap, "unknown execution flags 0x%x", flags);
     if (graph && job_ms) return fail(JR_EINVAL, err, cap, "per-job timing is not available with graph replay");
+    if (graph && streams) return fail(JR_EINVAL, err, cap, "graph replay and dependency-scheduled streams cannot be combined");
     auto *ctx = static_cast<Context *>(handle);
     if (!ctx) return fail(JR_EINVAL, err, cap, "null runtime context");
     int rc = validate_dispatch(ctx, jobs, job_count, err, cap);
@@ -537,6 +544,19 @@ extern "C" int jr_execute2(void *handle, const jr_dispatch *jobs, size_t job_cou
             if (st != cudaSuccess) return cuda_fail(st, err, cap, "create job events");
             ctx->job_events.push_back(e);
         }
+    }
+    if (streams) {
+        const size_t need = job_count * repeats;
+        if (need > 65536) return fail(JR_EINVAL, err, cap, "dependency-scheduled streams support at most 65536 job launches per call");
+        cudaError_t st = cudaSuccess;
+        if (!ctx->copy_in) st = cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking);
+        if (st == cudaSuccess && !ctx->copy_out) st = cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking);
+        while (st == cudaSuccess && ctx->dep_events.size() < need) {
+            cudaEvent_t e;
+            st = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+            if (st == cudaSuccess) ctx->dep_events.push_back(e);
+        }
+        if (st != cudaSuccess) return cuda_fail(st, err, cap, "create transfer streams/dependency events");
     }
     cudaError_t status;
     cudaGraphExec_t exec = nullptr;
@@ -559,20 +579,84 @@ extern "C" int jr_execute2(void *handle, const jr_dispatch *jobs, size_t job_cou
     }
     status = cudaEventRecord(ctx->start, ctx->stream);
     if (status != cudaSuccess) return cuda_fail(status, err, cap, "record start event");
+    // JR_EXEC_STREAMS: stream 0 = context stream, 1 = transfers in, 2 = transfers out.
+    // Per buffer, the last writing launch and the last reading launch on each stream
+    // since that write (launches on one stream are ordered, so the last one suffices).
+    struct Access {
+        long write = -1;
+        long read[3] = {-1, -1, -1};
+    };
+    std::map<const void *, Access> access;
+    std::vector<int> launch_stream;
+    long waited[3][3];  // [stream][source stream]: latest launch already waited for
+    long last_on[3] = {-1, -1, -1};
+    cudaStream_t stream_of[3] = {ctx->stream, ctx->copy_in, ctx->copy_out};
+    if (streams) {
+        for (auto &w : waited)
+            for (long &x : w) x = -1;
+        launch_stream.reserve(job_count * repeats);
+        status = cudaStreamWaitEvent(ctx->copy_in, ctx->start, 0);
+        if (status == cudaSuccess) status = cudaStreamWaitEvent(ctx->copy_out, ctx->start, 0);
+    }
     size_t ev = 0;
+    long launch = 0;
     for (uint32_t r = 0; r < repeats && status == cudaSuccess; ++r) {
         if (graph) {
             status = cudaGraphLaunch(exec, ctx->stream);
             continue;
         }
         for (size_t j = 0; j < job_count; ++j) {
-            if (job_ms) cudaEventRecord(ctx->job_events[ev++], ctx->stream);
-            status = jobs[j].kernel->run(ctx->stream, jobs[j].buffers);
-            if (job_ms) cudaEventRecord(ctx->job_events[ev++], ctx->stream);
+            int sid = 0;
+            if (streams) {
+                const jade::Spec &sp = jobs[j].kernel->spec;
+                if (sp.op == jade::Op::Copy) sid = sp.direction == "h2d" ? 1 : sp.direction == "d2h" ? 2 : 0;
+                long need[3] = {-1, -1, -1};
+                const auto &binds = jobs[j].kernel->binds;
+                for (size_t b = 0; b < binds.size(); ++b) {
+                    const Access &a = access[jobs[j].buffers[b]];
+                    if (a.write >= 0) need[launch_stream[a.write]] = std::max(need[launch_stream[a.write]], a.write);
+                    if (binds[b].write)
+                        for (int t = 0; t < 3; ++t) need[t] = std::max(need[t], a.read[t]);
+                }
+                for (int t = 0; t < 3 && status == cudaSuccess; ++t)
+                    if (t != sid && need[t] > waited[sid][t]) {
+                        status = cudaStreamWaitEvent(stream_of[sid], ctx->dep_events[need[t]], 0);
+                        waited[sid][t] = need[t];
+                    }
+                if (status != cudaSuccess) break;
+            }
+            cudaStream_t st = stream_of[sid];
+            if (job_ms) cudaEventRecord(ctx->job_events[ev++], st);
+            status = jobs[j].kernel->run(st, jobs[j].buffers);
+            if (job_ms) cudaEventRecord(ctx->job_events[ev++], st);
             if (status != cudaSuccess) break;
+            if (streams) {
+                status = cudaEventRecord(ctx->dep_events[launch], st);
+                launch_stream.push_back(sid);
+                last_on[sid] = launch;
+                const auto &binds = jobs[j].kernel->binds;
+                for (size_t b = 0; b < binds.size(); ++b) {
+                    Access &a = access[jobs[j].buffers[b]];
+                    if (binds[b].write) {
+                        a.write = launch;
+                        a.read[0] = a.read[1] = a.read[2] = -1;
+                    } else {
+                        a.read[sid] = launch;
+                    }
+                }
+                ++launch;
+                if (status != cudaSuccess) break;
+            }
         }
     }
+    if (streams)  // the context stream joins the transfer streams before the stop event
+        for (int t = 1; t < 3 && status == cudaSuccess; ++t)
+            if (last_on[t] >= 0) status = cudaStreamWaitEvent(ctx->stream, ctx->dep_events[last_on[t]], 0);
     if (status != cudaSuccess) {
+        if (streams) {
+            cudaStreamSynchronize(ctx->copy_in);
+            cudaStreamSynchronize(ctx->copy_out);
+        }
         cudaStreamSynchronize(ctx->stream);
         if (exec) cudaGraphExecDestroy(exec);
         if (g) cudaGraphDestroy(g);

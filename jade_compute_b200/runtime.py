@@ -26,6 +26,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include", "jade_runtime.h")
 
 JR_OK, JR_EINVAL, JR_ECUDA, JR_ENOMEM, JR_ETIMEOUT = 0, 1, 2, 3, 4
 JR_EXEC_GRAPH = 1
+JR_EXEC_STREAMS = 2
 
 DTYPE_SIZE = {"fp32": 4, "tf32": 4, "bf16": 2, "fp16": 2, "u8": 1}
 NP_DTYPE = {"fp32": np.float32, "tf32": np.float32, "bf16": np.uint16, "fp16": np.float16, "u8": np.uint8}
@@ -336,10 +337,13 @@ class Runtime:
         self._kernels.append(k)
         return k
 
-    def execute(self, jobs: Iterable, repeats: int = 1, graph: bool = False, per_job: bool = False) -> Execution:
+    def execute(self, jobs: Iterable, repeats: int = 1, graph: bool = False, per_job: bool = False,
+                streams: bool = False) -> Execution:
         """Ordered batch (corex.rs:544-612): every job is validated before any is
         launched; the sequence is replayed ``repeats`` times; returns host and
-        device times. ``jobs`` holds (Kernel, [Buffer, ...]) pairs."""
+        device times. ``jobs`` holds (Kernel, [Buffer, ...]) pairs. ``streams``
+        (JR_EXEC_STREAMS) runs transfer jobs on their own streams, ordered only by
+        the data dependencies of their bindings."""
         jobs = list(jobs)
         if not jobs or repeats <= 0:
             raise JadeError(JR_EINVAL, "execution requires jobs and positive repeats")
@@ -359,8 +363,8 @@ class Runtime:
         gpu = ctypes.c_double(0)
         jm = (ctypes.c_double * len(jobs))() if per_job else None
         t0 = time.perf_counter()
-        rc = lib().jr_execute2(self.ctx, disp, len(jobs), repeats, JR_EXEC_GRAPH if graph else 0, ctypes.byref(gpu),
-                               jm, e, len(e))
+        flags = (JR_EXEC_GRAPH if graph else 0) | (JR_EXEC_STREAMS if streams else 0)
+        rc = lib().jr_execute2(self.ctx, disp, len(jobs), repeats, flags, ctypes.byref(gpu), jm, e, len(e))
         host_ms = (time.perf_counter() - t0) * 1e3
         _check(rc, e)
         return Execution(host_ms, gpu.value if gpu.value > 0 else None, len(jobs) * repeats, repeats,

@@ -238,6 +238,36 @@ def test_row_kernels(rt, rows, cols, dtype):
     assert rc == 0
 
 
+@pytest.mark.parametrize("rows,cols,dtype,path", [(2000, 8192, "bf16", "row_staged_"), (3001, 4096, "bf16", "row_staged_"),
+                                                  (700, 32768, "bf16", "row_staged_"), (1500, 2048, "bf16", "row_staged_"),
+                                                  (2000, 8192, "fp32", "row_register_"), (700, 16384, "fp32", "row_register_")])
+def test_row_kernels_many_rows(rt, rows, cols, dtype, path):
+    # many rows per CTA: 16-bit rows staged through shared memory by bulk copies
+    # (several rows per ring position), FP32 rows register-resident (the kernel
+    # name says which path ran)
+    x = rt.alloc(rows * cols, dtype)
+    w = rt.alloc(cols, dtype)
+    rt.fill(x, "normal", seed=5, lo=0.0, hi=2.0)
+    rt.fill(w, "uniform", seed=5, stream=1, lo=0.5, hi=1.5)
+    xf, wf = rt.download_f32(x), rt.download_f32(w)
+    y, p, inv = rt.alloc(rows * cols, dtype), rt.alloc(rows * cols, dtype), rt.alloc(rows)
+    base = {"rows": rows, "cols": cols, "dtype": dtype}
+    kerns = [rt.compile({"op": "rms_norm", "epsilon": 1e-6, **base}), rt.compile({"op": "softmax", **base}),
+             rt.compile({"op": "rms_inv", "epsilon": 1e-6, **base})]
+    for k in kerns:
+        assert k.info["impl"].startswith(path), k.info
+    rt.execute([(kerns[0], [x, w, y]), (kerns[1], [x, p]), (kerns[2], [x, inv])], repeats=2)
+    eps = float(np.float32(1e-6))
+    tol = 3e-5 if dtype == "fp32" else 2 ** -8
+    rc, r = O.compare(rt.download_f32(y), O.normalize(rows, cols, xf, wf, eps), tol, tol)
+    assert rc == 0, r.max_abs_error
+    rc, r = O.compare(rt.download_f32(p), O.softmax(rows, cols, xf), tol, tol)
+    assert rc == 0, r.max_abs_error
+    X = xf.reshape(rows, cols).astype(np.float64)
+    rc, _ = O.compare(rt.download(inv), 1 / np.sqrt((X * X).mean(1) + eps), 3e-5, 3e-5)
+    assert rc == 0
+
+
 def test_softmax_stress_rows(rt):
     # BASELINE config 3 scales logits by 4; extreme rows as workloads.rs:125-133
     rows, cols = 4, 8192
@@ -293,6 +323,34 @@ def test_per_job_timing_and_copy_jobs(rt):
     assert len(t.job_ms) == 3 and all(x > 0 for x in t.job_ms)
     with pytest.raises(JadeError):  # device buffer where a pinned host buffer is required
         rt.execute([(h2d, [d, e])])
+
+
+def test_dependency_scheduled_streams_keep_order(rt):
+    # JR_EXEC_STREAMS: transfers on their own streams, ordered by the data hazards
+    # of their bindings only. Two rounds reuse the same device buffers, so every
+    # kind of hazard appears: the second upload into d must wait for the first
+    # add to read d (write after read), the second add into e for the first
+    # read-back of e (write after read) and the read-backs for their adds (read
+    # after write). 64 MB buffers make a violated order visible in the results.
+    n = 1 << 24
+    h1, h2, o1, o2 = (rt.host_alloc(n) for _ in range(4))
+    h1.host_view()[:] = np.arange(n, dtype=np.float32)
+    h2.host_view()[:] = -np.arange(n, dtype=np.float32) - 1
+    d, e = rt.alloc(n), rt.alloc(n)
+    h2d = rt.compile({"op": "copy", "bytes": 4 * n, "direction": "h2d"})
+    d2h = rt.compile({"op": "copy", "bytes": 4 * n, "direction": "d2h"})
+    add = rt.compile({"op": "add", "len": n})
+    jobs = [(h2d, [h1, d]), (add, [d, d, e]), (d2h, [e, o1]), (h2d, [h2, d]), (add, [d, d, e]), (d2h, [e, o2])]
+    for rep in range(3):
+        o1.host_view()[:] = 0
+        o2.host_view()[:] = 0
+        t = rt.execute(jobs, repeats=2, streams=True, per_job=(rep == 2))
+        assert np.array_equal(o1.host_view(), 2 * np.arange(n, dtype=np.float32))
+        assert np.array_equal(o2.host_view(), -2 * np.arange(n, dtype=np.float32) - 2)
+        assert t.gpu_ms > 0
+    assert len(t.job_ms) == 6 and all(x > 0 for x in t.job_ms)
+    with pytest.raises(JadeError, match="cannot be combined"):
+        rt.execute(jobs, streams=True, graph=True)
 
 
 def test_fill_is_deterministic_and_distributed(rt):
