@@ -30,8 +30,8 @@
 //              if step j-1 moved it or row j's maximum grows by more than 2^8
 //              (then O is rescaled in place after P(j-1).V(j-1) has landed).
 //              P(j) (16-bit pairs) is written over the first 64 columns of S(j).
-// A small fixed share of the exponentials of unmasked tiles is evaluated with a
-// cubic polynomial on the FMA pipe instead of the MUFU unit.
+// Every exponential runs on the MUFU unit: moving a share of them to the FMA-pipe
+// polynomial (as the two-tile kernel does) measured 0.6-1% slower here.
 // Short waits poll (mbarrier.test_wait) instead of suspending: a suspended
 // waiter resumes a few hundred cycles after the phase completes.
 // Every wait is bounded (the error word records where it gave up); every thread
@@ -496,8 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!(ok = __all_sync(0xffffffffu, mbar_spin(&s_full[b], (g / 3) & 1, abort_flag, err, kErrWaitScore)))) break;
                 const float m_tile = load_row_max(sv, ts, j * kKeys, q0, q, args.seq, args.causal, c);
-                const int k0 = j * kKeys;
-                const bool need_mask = (args.causal && k0 + kKeys - 1 > q0) || (k0 + kKeys > args.seq);
                 // the maximum published by step g-1 of this item (the other warp's)
                 auto read_prev = [&]() {
                     if (!__all_sync(0xffffffffu, mbar_spin(&pub[quarter * 2 + (par ^ 1)], ((g - 1) >> 1) & 1, abort_flag, err, kErrWaitScore)))
@@ -516,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                     if (j == 1) m_view = fmaxf(m_tile, m_pre);  // equals what step 0 publishes
                     const float m_spec = m_view;
-                    psum = need_mask ? store_p<kFmt, false, kCols>(sv, c, m_spec, ts) : store_p<kFmt, kFmt == 1, kCols>(sv, c, m_spec, ts);
+                    psum = store_p<kFmt, false, kCols>(sv, c, m_spec, ts);  // all exponentials on MUFU (measured best here)
                     if (!(ok = read_prev())) break;
                     fresh = __all_sync(0xffffffffu, m_view == m_spec);
                 }
