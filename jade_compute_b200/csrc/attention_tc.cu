@@ -482,7 +482,9 @@ LaunchFn attn_launch(Context *ctx, const Spec &s) {
     base.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
     base.err = ctx->err_dev;
     base.bh_total = heads_total;
-    base.group_heads = (int)std::max<long long>(1, std::min<long long>(heads_total, (64ll << 20) / (4ll * (long long)s.seq * D)));
+    // K/V of a head group in 32 MB of L2 (measured against 16, 48 and 64 MB: the
+    // persistent CTAs drift apart and work on two groups at once near a boundary)
+    base.group_heads = attention_group_heads(heads_total, s.seq, D, 32ll << 20);
     if ((long long)heads_total * base.npairs > INT_MAX) throw IrError("attention too large for one launch");
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, L::kSmem) != cudaSuccess || per_sm < 1)

@@ -57,6 +57,9 @@ constexpr int kStages = 3;     // K and V ring depth (V loads trail K by one ste
 // other the odd ones, each thread a whole row (128 scores) of its steps
 constexpr int kCols = kKeys;
 constexpr int kThreads = 10 * 32;
+#ifndef PAIR_GROUP_BYTES
+#define PAIR_GROUP_BYTES (64ll << 20)
+#endif
 constexpr int kMaxItems = 512;   // work items per CTA pair (the host checks the bound)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -653,8 +656,8 @@ bool make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64_
 template <typename TIn, typename TOut>
 LaunchFn pair_launch(Context *ctx, const Spec &s) {
     const long long heads_all = (long long)s.batch * s.heads;
-    // heads whose K and V (2 x seq x 128 x 2 bytes each) fit in about 64 MB of the 126 MB L2
-    const int group_heads = (int)std::max<long long>(1, std::min<long long>(heads_all, (64ll << 20) / (4ll * (long long)s.seq * kDim)));
+    // heads whose K and V fit in about 64 MB of the 126 MB L2, in even groups
+    const int group_heads = attention_group_heads(heads_all, s.seq, kDim, PAIR_GROUP_BYTES);
     const bool grouped = group_heads < heads_all;
     auto kernel = grouped ? attention_pair_kernel<TIn, TOut, true> : attention_pair_kernel<TIn, TOut, false>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Layout::kSmem) != cudaSuccess)

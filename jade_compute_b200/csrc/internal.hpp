@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <functional>
@@ -68,6 +69,14 @@ bool gemm_tc_supports(const Spec &s, std::string &why);
 LaunchFn make_attention_simt(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_attention_tc(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_attention_pair(Context *ctx, const Spec &s, std::string &impl);  // dim 128, CTA pairs
+// Heads per group of the attention work order: groups whose K and V (2 x seq x dim
+// x 2 bytes per head) fit in `budget` bytes of L2, split evenly (64 heads under a
+// budget for 48 run as 32 + 32, not 48 + 16: a small last group leaves workers idle).
+inline int attention_group_heads(long long heads, long long seq, long long dim, long long budget) {
+    const long long fit = std::max<long long>(1, budget / (4 * seq * dim));
+    const long long groups = (heads + fit - 1) / fit;
+    return (int)((heads + groups - 1) / groups);
+}
 // Which 16-bit attention kernel to run, from measurements on B200. Both deal
 // (head, 256-query) work items to persistent workers: the two-tile kernel to one
 // CTA per SM, the pair kernel to one CTA pair per two SMs. The two-tile kernel has
