@@ -14,9 +14,11 @@ Contract (one JSON line on rank 0):
              measured dense BF16 peak; traffic from the committed ncu summary.
   cpu_baseline  the FP64 oracle (the reference's CPU attention restated,
              metal_lab.rs:33-73) on a bounded sample of rows, all host threads.
-  components GEMM 8192^3 BF16 split by output columns over the ranks, the
-             residual MLP block (tensor parallel with one
-             NCCL all-reduce), non-causal attention.
+  components the row kernels and the lowered IR expression (
+             each with the SM clocks of its own timed region), GEMM 8192^3 BF16
+             split by output columns over the ranks, the residual MLP block
+             (tensor parallel with one NCCL all-reduce),
+             non-causal attention.
 Multi-GPU: one process per GPU (torchrun); each rank runs its own batch x head
 shard of the headline attention (weak scaling, no collective on the data path).
 
@@ -232,7 +234,7 @@ def gemm_bench(rt, dist, world, steps, warmup, m=8192):
             "impl": g.info.get("impl")}
 
 
-def row_benches(rt, steps, warmup, peaks):
+def row_benches(rt, steps, warmup, peaks, device=0):
     """RMSNorm and softmax on 16384 x 8192 (FP32 and BF16,
     RMSNorm eps 1e-6, weight U[0.5,1.5], softmax logits N(0,1)*4), and the IR
     expression max(2.5x+y, 0) over 2^28 FP32 elements. HBM-bound: algorithmic
@@ -253,13 +255,14 @@ def row_benches(rt, steps, warmup, peaks):
             k = rt.compile(spec)
             jobs = [(flush, [flush_buf]), (k, bufs)]
             rt.execute(jobs, repeats=max(warmup, 3))
-            t = rt.execute(jobs, repeats=steps, per_job=True)
+            with ClockSampler(device) as clk:
+                t = rt.execute(jobs, repeats=steps, per_job=True)
             ms = t.job_ms[1] / steps
             gbs = nbytes / (ms * 1e-3) / 1e9
             out.append({"workload": f"{op} {R}x{C} {dtype} (BASELINE configs[2])", "value": gbs, "unit": "GB/s",
                         "ms_per_step": ms, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
                                                         "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"]},
-                        "impl": k.info.get("impl")})
+                        "impl": k.info.get("impl"), "clocks": clk.summary()})
         for b in (x, y, w):
             b.free()
     a, b, c = rt.alloc(n_expr), rt.alloc(n_expr), rt.alloc(n_expr)
@@ -272,12 +275,13 @@ def row_benches(rt, steps, warmup, peaks):
     k = rt.compile({"op": "elementwise", "len": n_expr, "inputs": 2, "expression": expr})
     jobs = [(flush, [flush_buf]), (k, [a, b, c])]
     rt.execute(jobs, repeats=max(warmup, 3))
-    t = rt.execute(jobs, repeats=steps, per_job=True)
+    with ClockSampler(device) as clk:
+        t = rt.execute(jobs, repeats=steps, per_job=True)
     ms = t.job_ms[1] / steps
     gbs = 3 * 4 * n_expr / (ms * 1e-3) / 1e9
     out.append({"workload": "elementwise max(2.5x+y,0) over 2^28 fp32 (BASELINE configs[2])", "value": gbs, "unit": "GB/s",
                 "ms_per_step": ms, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                                                "frac": gbs / peaks["hbm_gbs"]}, "impl": k.info.get("impl")})
+                                                "frac": gbs / peaks["hbm_gbs"]}, "impl": k.info.get("impl"), "clocks": clk.summary()})
     for x in (a, b, c, flush_buf):
         x.free()
     return out
@@ -379,7 +383,7 @@ def run_only(args):
         elif w == "mlp":
             res = mlp_bench(rt, dist, world, args.steps, args.warmup, peaks)
         elif w == "rows":
-            res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks)}
+            res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks, local)}
         elif w == "sweep":
             res = {"workload": "sweep", "components": sweep(rt, dist, world, rank, args.steps, args.warmup, peaks)}
         else:
@@ -428,14 +432,19 @@ def run_ours(args):
         e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
         components = []
         if not args.quick:
-            components.append(gemm_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup))
-            components.append(mlp_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks))
-            components.extend(row_benches(rt, max(5, min(args.steps, 20)), args.warmup, peaks))
+            # row kernels and non-causal attention before the ~1 kW GEMM and MLP: measured
+            # right after those, they ran 10-28% slower (partly issue-bound, they follow
+            # the SM clock); each of them records the clocks of its own timed region
+            components.extend(row_benches(rt, max(5, min(args.steps, 20)), args.warmup, peaks, local))
             jobs_f, attn_f, bufs_f, fb = attention_bench(rt, jc, args.steps, args.warmup, False, B)
-            tf = rt.execute(jobs_f, repeats=max(5, min(args.steps, 50)), per_job=True)
+            with ClockSampler(local) as clk_f:
+                tf = rt.execute(jobs_f, repeats=max(5, min(args.steps, 50)), per_job=True)
             ms_f = tf.job_ms[1] / max(5, min(args.steps, 50))
             components.append({"workload": f"non-causal attention B={B} H={H} S={S} D={D} BF16", "unit": "TFLOP/s",
-                               "value": full_flops(B, H, S, D) / (ms_f * 1e-3) / 1e12, "ms_per_step": ms_f})
+                               "value": full_flops(B, H, S, D) / (ms_f * 1e-3) / 1e12, "ms_per_step": ms_f,
+                               "impl": attn_f.info.get("impl"), "clocks": clk_f.summary()})
+            components.append(gemm_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup))
+            components.append(mlp_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks))
         cpu = None
         if rank == 0 and not args.no_cpu:
             from oracle import oracle as O
