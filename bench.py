@@ -316,30 +316,13 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks):
     return out
 
 
-def sweep(rt, dist, world, rank, steps, warmup, peaks):
+def sweep(rt, dist, world, rank, steps, warmup, peaks, device=0):
     """BASELINE config 5 on this box: BF16 and TF32 square GEMMs M=N=K in
     {1k..16k} split by output columns over the ranks, and causal attention B=8,
     H=32, D=128, S in {4k, 8k, 16k} split by batch x head (B*H/world heads per rank)."""
     from jade_compute_b200 import parallel
     out = []
-    for dtype in ("bf16", "tf32"):
-        for m in (1024, 2048, 4096, 8192, 16384):
-            cols = parallel.split_range(m, world, rank)
-            n = len(cols)
-            a, b, c = rt.alloc(m * m, dtype), rt.alloc(n * m, dtype), rt.alloc(m * n, "fp32")
-            rt.fill(a, "uniform", seed=7, stream=0, lo=-1, hi=1)
-            rt.fill(b, "uniform", seed=7, stream=1 + rank, lo=-1, hi=1)
-            g = rt.compile({"op": "gemm", "m": m, "n": n, "k": m, "tiled": True, "dtype": dtype, "b_layout": "nk"})
-            reps = max(3, min(steps, int(2e13 / (2.0 * m ** 3)) + 1))
-            rt.execute([(g, [a, b, c])], repeats=max(warmup, 2))
-            barrier(dist)
-            t = rt.execute([(g, [a, b, c])], repeats=reps, per_job=True)
-            ms = reduce_max(dist, t.job_ms[0] / reps)
-            tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
-            out.append({"workload": f"GEMM {m}^3 {dtype} (FP32 out), N-split x{world}", "value": tf, "unit": "TFLOP/s",
-                        "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"], "impl": g.info.get("impl")})
-            for x in (a, b, c):
-                x.free()
+    # attention first: after the long GEMMs (power-capped) the SM clock recovers slowly
     Bs, Hs = 8, 32
     for seq in (4096, 8192, 16384):
         heads = parallel.split_range(Bs * Hs, world, rank)
@@ -352,14 +335,35 @@ def sweep(rt, dist, world, rank, steps, warmup, peaks):
         rt.execute([(attn, [q, k, v, o])], repeats=max(warmup, 2))
         barrier(dist)
         reps = max(3, min(steps, 20))
-        t = rt.execute([(attn, [q, k, v, o])], repeats=reps, per_job=True)
+        with ClockSampler(device) as clk:
+            t = rt.execute([(attn, [q, k, v, o])], repeats=reps, per_job=True)
         ms = reduce_max(dist, t.job_ms[0] / reps)
         tf = causal_flops(Bs, Hs, seq, D) / (ms * 1e-3) / 1e12
         out.append({"workload": f"causal attention B={Bs} H={Hs} S={seq} D={D} BF16, batch x head split x{world}",
                     "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"],
-                    "impl": attn.info.get("impl")})
+                    "impl": attn.info.get("impl"), "clocks": clk.summary()})
         for x in (q, k, v, o):
             x.free()
+    for dtype in ("bf16", "tf32"):
+        for m in (1024, 2048, 4096, 8192, 16384):
+            cols = parallel.split_range(m, world, rank)
+            n = len(cols)
+            a, b, c = rt.alloc(m * m, dtype), rt.alloc(n * m, dtype), rt.alloc(m * n, "fp32")
+            rt.fill(a, "uniform", seed=7, stream=0, lo=-1, hi=1)
+            rt.fill(b, "uniform", seed=7, stream=1 + rank, lo=-1, hi=1)
+            g = rt.compile({"op": "gemm", "m": m, "n": n, "k": m, "tiled": True, "dtype": dtype, "b_layout": "nk"})
+            reps = max(3, min(steps, int(2e13 / (2.0 * m ** 3)) + 1))
+            rt.execute([(g, [a, b, c])], repeats=max(warmup, 2))
+            barrier(dist)
+            with ClockSampler(device) as clk:
+                t = rt.execute([(g, [a, b, c])], repeats=reps, per_job=True)
+            ms = reduce_max(dist, t.job_ms[0] / reps)
+            tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
+            out.append({"workload": f"GEMM {m}^3 {dtype} (FP32 out), N-split x{world}", "value": tf, "unit": "TFLOP/s",
+                        "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"], "impl": g.info.get("impl"),
+                        "clocks": clk.summary()})
+            for x in (a, b, c):
+                x.free()
     return out
 
 
@@ -385,7 +389,7 @@ def run_only(args):
         elif w == "rows":
             res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks, local)}
         elif w == "sweep":
-            res = {"workload": "sweep", "components": sweep(rt, dist, world, rank, args.steps, args.warmup, peaks)}
+            res = {"workload": "sweep", "components": sweep(rt, dist, world, rank, args.steps, args.warmup, peaks, local)}
         else:
             raise SystemExit(f"unknown workload {w}")
         if rank == 0:
