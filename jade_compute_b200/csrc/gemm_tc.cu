@@ -35,7 +35,9 @@ namespace {
 
 constexpr int BM = 128, BN = 256, kStages = 4, kThreads = 192;
 constexpr uint32_t kStageA = BM * 128, kStageB = BN * 128, kStageBytes = kStageA + kStageB;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+// per epilogue warp: a 32 x 32 FP32 block padded to 33 columns (transposes its stores)
+constexpr uint32_t kEpiBlock = 32 * 33 * 4, kEpiBytes = 4 * kEpiBlock;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 256 /*barriers*/ + kEpiBytes + 1024 /*align*/;
 
 enum Epi { kEpiNone = 0, kEpiSwiglu = 1, kEpiResidual = 2 };
 
@@ -95,6 +97,23 @@ __device__ __forceinline__ void store32_16(T16 *dst, const float (&v)[32], int v
 template <>
 __device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16 *dst, const float (&v)[32], int valid, bool vec_ok) {
     store32_16(dst, v, valid, vec_ok);
+}
+// Four consecutive values of a row (16 B of FP32, 8 B of 16-bit types).
+template <typename TOut>
+__device__ __forceinline__ void store4(TOut *dst, const float (&v)[4], int valid, bool vec_ok) {
+    if (valid >= 4 && vec_ok) {
+        if constexpr (std::is_same<TOut, float>::value) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        } else if constexpr (std::is_same<TOut, __nv_bfloat16>::value) {
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+        } else {
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (e < valid) dst[e] = from_f32<TOut>(v[e]);
+    }
 }
 template <>
 __device__ __forceinline__ void store32<__half>(__half *dst, const float (&v)[32], int valid, bool vec_ok) {
@@ -244,7 +263,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         store32<TOut>(out + (size_t)row * args.N + col, h, args.N - col, (args.N % 8) == 0);
                 }
             } else {
-                const int c0 = tn * BN;
+                // The warp's 32 rows x 32 columns go through its padded shared-memory
+                // block, so that each store instruction writes 4 rows x 32 columns
+                // (row-contiguous) instead of 32 rows x 4 columns: a thread-per-row
+                // store touches 32 cache lines per instruction and made the epilogue
+                // of a 128 x 256 FP32 tile take ~5 us.
+                float *blk = reinterpret_cast<float *>(smem + kStages * kStageBytes + 256) + (warp - 2) * (32 * 33);
+                const int c0 = tn * BN, row0 = tm * BM + quarter * 32;
+                const int r_sub = lane >> 3, c_sub = (lane & 7) * 4;  // this lane's row in each group of 4, its columns
+                const bool vec_ok = (args.N % 4) == 0;
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 32) {
                     const int col = c0 + c;
@@ -252,18 +279,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t r[32];
                     tmem_ld32(tbase + c, r);
                     tmem_wait_ld();
-                    float v[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
-                    if (row < args.M) {
-                        if constexpr (kEpi == kEpiResidual) {
-                            const TOut *res = static_cast<const TOut *>(args.residual) + (size_t)row * args.N + col;
+                    for (int j = 0; j < 32; ++j) blk[lane * 33 + j] = __uint_as_float(r[j]) * scale;
+                    __syncwarp();
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col + j < args.N) v[j] += to_f32(res[j]);
+                    for (int i = 0; i < 8; ++i) {
+                        const int rl = i * 4 + r_sub, grow = row0 + rl, gcol = col + c_sub;
+                        if (grow < args.M && gcol < args.N) {
+                            float v[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) v[e] = blk[rl * 33 + c_sub + e];
+                            if constexpr (kEpi == kEpiResidual) {
+                                const TOut *res = static_cast<const TOut *>(args.residual) + (size_t)grow * args.N + gcol;
+#pragma unroll
+                                for (int e = 0; e < 4; ++e)
+                                    if (gcol + e < args.N) v[e] += to_f32(res[e]);
+                            }
+                            store4<TOut>(out + (size_t)grow * args.N + gcol, v, args.N - gcol, vec_ok);
                         }
-                        store32<TOut>(out + (size_t)row * args.N + col, v, args.N - col, (args.N % 8) == 0);
                     }
+                    __syncwarp();  // the block is read before the next chunk overwrites it
                 }
             }
             tc_fence_before();
