@@ -157,14 +157,16 @@ JR_API int jr_comm_destroy(void *ctx);
  *
  *  - Limit: k * n <= 4,194,304 elements (16 MiB of FP32); larger shapes are
  *    rejected with JR_EINVAL and a message. k must be a multiple of 4 and a, b
- *    16-byte aligned. Every GPU that loads the library holds the 16 MiB until
- *    the process exits.
+ *    and out 16-byte aligned (rejected with JR_EINVAL before any launch
+ *    otherwise). Every GPU that loads the library holds the 16 MiB until the
+ *    process exits.
  *  - Runs on the current device. The first call on each device performs a
  *    one-time set-up there (it looks up the array's device address); make that
  *    first call before any stream capture.
  *  - Enqueues on `stream` (NULL = the legacy default stream) and synchronises
- *    it before returning; returns JR_ETIMEOUT if a device-side bounded wait
- *    expired.
+ *    that stream before returning (the error word is read back on it too, so
+ *    no other stream is synchronised); returns JR_ETIMEOUT if a device-side
+ *    bounded wait expired.
  *  - Every call on a device shares the one array and it keeps the last call's
  *    contents: calls whose GPU work overlaps (several host threads or streams at
  *    once) race on it and must be serialised by the caller. */

@@ -9,11 +9,12 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
-#include <cstdarg>
-#include <cstdio>
+#include <algorithm>
 #include <cstring>
+#include <vector>
 
 #include "../../include/jade_runtime.h"
+#include "cabi.hpp"
 #include "internal.hpp"
 
 namespace jade {
@@ -54,36 +55,28 @@ Nccl &nccl() {
     return n;
 }
 
-int fail(int code, char *err, size_t cap, const char *format, ...) {
-    if (err && cap) {
-        va_list args;
-        va_start(args, format);
-        std::vsnprintf(err, cap, format, args);
-        va_end(args);
-        err[cap - 1] = '\0';
-    }
-    return code;
-}
 const char *nccl_str(ncclResult_t r) { return nccl().error_string ? nccl().error_string(r) : "nccl error"; }
-int need_nccl(char *err, size_t cap) {
+void need_nccl() {
     Nccl &n = nccl();
-    if (!n.lib || !n.get_unique_id || !n.init_rank || !n.all_reduce || !n.abort)
-        return fail(JR_EINVAL, err, cap, "NCCL (libnccl.so.2) is not available");
-    return 0;
+    require(n.lib && n.get_unique_id && n.init_rank && n.all_reduce && n.abort, "NCCL (libnccl.so.2) is not available");
+}
+void check_nccl(ncclResult_t r, const char *operation) {
+    if (r != ncclSuccess) raise(JR_ECUDA, "%s: %s", operation, nccl_str(r));
 }
 
 }  // namespace
 
-int comm_poll_abort(Context *ctx, char *err, size_t cap) {
-    if (!ctx->nccl_comm || !nccl().async_error) return 0;
+// Throws JR_ETIMEOUT (after aborting the communicator) when NCCL reports an
+// asynchronous error for this context's communicator.
+void comm_poll_abort(Context *ctx) {
+    if (!ctx->nccl_comm || !nccl().async_error) return;
     ncclResult_t async = ncclSuccess;
     nccl().async_error(static_cast<ncclComm_t>(ctx->nccl_comm), &async);
     if (async != ncclSuccess && async != ncclInProgress) {
         nccl().abort(static_cast<ncclComm_t>(ctx->nccl_comm));
         ctx->nccl_comm = nullptr;
-        return fail(JR_ETIMEOUT, err, cap, "collective failed asynchronously: %s; communicator aborted", nccl_str(async));
+        raise(JR_ETIMEOUT, "collective failed asynchronously: %s; communicator aborted", nccl_str(async));
     }
-    return 0;
 }
 
 void comm_destroy(Context *ctx) {
@@ -110,62 +103,58 @@ LaunchFn make_all_reduce(Context *ctx, const Spec &s, std::string &impl) {
 using jade::Context;
 
 extern "C" int jr_comm_unique_id(unsigned char id[128], char *err, size_t cap) {
-    if (err && cap) err[0] = '\0';
-    if (!id) return jade::fail(JR_EINVAL, err, cap, "null id buffer");
-    if (int rc = jade::need_nccl(err, cap)) return rc;
-    ncclUniqueId u;
-    const ncclResult_t r = jade::nccl().get_unique_id(&u);
-    if (r != ncclSuccess) return jade::fail(JR_ECUDA, err, cap, "ncclGetUniqueId: %s", jade::nccl_str(r));
-    static_assert(sizeof(u) == 128, "ncclUniqueId is 128 bytes");
-    memcpy(id, &u, 128);
-    return 0;
+    return jade::c_entry(err, cap, [&] {
+        jade::require(id != nullptr, "null id buffer");
+        jade::need_nccl();
+        ncclUniqueId u;
+        jade::check_nccl(jade::nccl().get_unique_id(&u), "ncclGetUniqueId");
+        static_assert(sizeof(u) == 128, "ncclUniqueId is 128 bytes");
+        memcpy(id, &u, 128);
+    });
 }
 
+namespace {
+void attach(Context *c, ncclComm_t comm, int nranks, int rank, uint32_t timeout_ms) {
+    c->nccl_comm = comm;
+    c->nranks = nranks;
+    c->rank = rank;
+    c->comm_timeout_ms = timeout_ms ? timeout_ms : 60000;
+}
+}  // namespace
+
 extern "C" int jr_comm_init(void *handle, int nranks, int rank, const unsigned char id[128], uint32_t timeout_ms, char *err, size_t cap) {
-    if (err && cap) err[0] = '\0';
-    auto *ctx = static_cast<Context *>(handle);
-    if (!ctx || !id) return jade::fail(JR_EINVAL, err, cap, "null context or id");
-    if (nranks < 1 || rank < 0 || rank >= nranks) return jade::fail(JR_EINVAL, err, cap, "rank %d outside communicator of %d ranks", rank, nranks);
-    if (ctx->nccl_comm) return jade::fail(JR_EINVAL, err, cap, "context already has a communicator");
-    if (int rc = jade::need_nccl(err, cap)) return rc;
-    if (cudaSetDevice(ctx->device) != cudaSuccess) return jade::fail(JR_ECUDA, err, cap, "cudaSetDevice");
-    ncclUniqueId u;
-    memcpy(&u, id, 128);
-    ncclComm_t comm = nullptr;
-    const ncclResult_t r = jade::nccl().init_rank(&comm, nranks, u, rank);
-    if (r != ncclSuccess) return jade::fail(JR_ECUDA, err, cap, "ncclCommInitRank: %s", jade::nccl_str(r));
-    ctx->nccl_comm = comm;
-    ctx->nranks = nranks;
-    ctx->rank = rank;
-    ctx->comm_timeout_ms = timeout_ms ? timeout_ms : 60000;
-    return 0;
+    return jade::c_entry(err, cap, [&] {
+        auto *ctx = static_cast<Context *>(handle);
+        jade::require(ctx && id, "null context or id");
+        if (nranks < 1 || rank < 0 || rank >= nranks) jade::raise(JR_EINVAL, "rank %d outside communicator of %d ranks", rank, nranks);
+        jade::require(!ctx->nccl_comm, "context already has a communicator");
+        jade::need_nccl();
+        jade::check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice");
+        ncclUniqueId u;
+        memcpy(&u, id, 128);
+        ncclComm_t comm = nullptr;
+        jade::check_nccl(jade::nccl().init_rank(&comm, nranks, u, rank), "ncclCommInitRank");
+        attach(ctx, comm, nranks, rank, timeout_ms);
+    });
 }
 
 extern "C" int jr_comm_init_all(void **ctxs, int count, uint32_t timeout_ms, char *err, size_t cap) {
-    if (err && cap) err[0] = '\0';
-    if (!ctxs || count < 1) return jade::fail(JR_EINVAL, err, cap, "no contexts");
-    if (int rc = jade::need_nccl(err, cap)) return rc;
-    if (!jade::nccl().init_all) return jade::fail(JR_EINVAL, err, cap, "ncclCommInitAll unavailable");
-    std::vector<int> devs(count);
-    for (int i = 0; i < count; ++i) {
-        auto *c = static_cast<Context *>(ctxs[i]);
-        if (!c) return jade::fail(JR_EINVAL, err, cap, "null context %d", i);
-        if (c->nccl_comm) return jade::fail(JR_EINVAL, err, cap, "context %d already has a communicator", i);
-        for (int j = 0; j < i; ++j)
-            if (devs[j] == c->device) return jade::fail(JR_EINVAL, err, cap, "device %d appears twice", c->device);
-        devs[i] = c->device;
-    }
-    std::vector<ncclComm_t> comms(count);
-    const ncclResult_t r = jade::nccl().init_all(comms.data(), count, devs.data());
-    if (r != ncclSuccess) return jade::fail(JR_ECUDA, err, cap, "ncclCommInitAll: %s", jade::nccl_str(r));
-    for (int i = 0; i < count; ++i) {
-        auto *c = static_cast<Context *>(ctxs[i]);
-        c->nccl_comm = comms[i];
-        c->nranks = count;
-        c->rank = i;
-        c->comm_timeout_ms = timeout_ms ? timeout_ms : 60000;
-    }
-    return 0;
+    return jade::c_entry(err, cap, [&] {
+        jade::require(ctxs && count >= 1, "no contexts");
+        jade::need_nccl();
+        jade::require(jade::nccl().init_all != nullptr, "ncclCommInitAll unavailable");
+        std::vector<int> devs;
+        for (int i = 0; i < count; ++i) {
+            auto *c = static_cast<Context *>(ctxs[i]);
+            if (!c) jade::raise(JR_EINVAL, "null context %d", i);
+            if (c->nccl_comm) jade::raise(JR_EINVAL, "context %d already has a communicator", i);
+            if (std::find(devs.begin(), devs.end(), c->device) != devs.end()) jade::raise(JR_EINVAL, "device %d appears twice", c->device);
+            devs.push_back(c->device);
+        }
+        std::vector<ncclComm_t> comms(count);
+        jade::check_nccl(jade::nccl().init_all(comms.data(), count, devs.data()), "ncclCommInitAll");
+        for (int i = 0; i < count; ++i) attach(static_cast<Context *>(ctxs[i]), comms[i], count, i, timeout_ms);
+    });
 }
 
 extern "C" int jr_comm_destroy(void *handle) {

@@ -1,90 +1,182 @@
-// Fixed-shape GEMM plan ABI (include/jade_corex.h): the reference's cuBLAS
-// provider contract (native/jade_corex.cpp:110-266) implemented on this
-// library's own kernels through its C ABI (jr_create / jr_compile /
-// jr_execute2). Validation order, error codes and messages follow the
-// reference; the GEMM is the FP32 FFMA kernel (precision 0) or the tcgen05
-// FP16 x FP16 -> FP32 kernel (precision 1).
+// Fixed-shape GEMM plan ABI (include/jade_corex.h), the drop-in for the
+// reference's cuBLAS provider (native/jade_corex.h, loaded by src/corex.rs:55-84).
+// A plan is a small object over this library's own C ABI: one jr context that
+// owns the stream, events and the A, B, C buffers, and one compiled GEMM - the
+// FP32 FFMA kernel (precision 0) or the tcgen05 FP16 x FP16 -> FP32 kernel
+// (precision 1, inputs rounded to FP16 on upload). The exported functions keep
+// the provider's symbols, validation order, result codes and message texts.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <climits>
 #include <cmath>
-#include <cstdarg>
 #include <cstdio>
-#include <limits>
+#include <memory>
 #include <new>
 #include <string>
 #include <vector>
 
+#include "cabi.hpp"
 #include "jade_corex.h"
 #include "jade_runtime.h"
 
 namespace {
 
-struct Plan {
-    uint32_t m = 0, n = 0, k = 0, precision = 0;
-    int device = 0;
-    size_t a_len = 0, b_len = 0, c_len = 0;
-    size_t a_bytes = 0, b_bytes = 0, c_bytes = 0;
-    void *rt = nullptr;  // jr context (owns the stream, events and buffers)
-    void *a = nullptr, *b = nullptr, *c = nullptr;
-    jr_kernel *kernel = nullptr;
-    std::vector<uint16_t> host_a, host_b;  // FP16 staging (precision 1)
-    bool uploaded = false, computed = false;
+// Result codes of this ABI (jade_corex.h): they differ from jr_*'s numbering.
+constexpr int kInvalid = 1, kRuntime = 2, kAllocation = 4;
+
+[[noreturn]] void invalid(const char *message) { throw jade::Fault{kInvalid, message}; }
+
+// Runs one jr_* call with a message buffer of its own; a failure is re-thrown in
+// this ABI's numbering with the runtime's message.
+template <class Call>
+void via_runtime(Call &&call) {
+    char message[512] = {0};
+    const int rc = call(message, sizeof message);
+    if (rc == JR_OK) return;
+    throw jade::Fault{rc == JR_EINVAL ? kInvalid : rc == JR_ENOMEM ? kAllocation : kRuntime, message};
+}
+
+// Element count and byte size of an x-by-y matrix of `width`-byte values.
+bool extent(uint64_t x, uint64_t y, size_t width, size_t &count, size_t &bytes) {
+    return !__builtin_mul_overflow(x, y, &count) && !__builtin_mul_overflow(count, width, &bytes);
+}
+
+class Plan {
+  public:
+    Plan(uint32_t m, uint32_t n, uint32_t k, int device, uint32_t precision)
+        : m_(m), n_(n), k_(k), device_(device), fp16_(precision == 1) {
+        const size_t in = fp16_ ? sizeof(uint16_t) : sizeof(float);
+        size_t host_a = 0, host_b = 0;  // the caller's FP32 arrays must be addressable too
+        if (!extent(m, k, in, a_.count, a_.bytes) || !extent(k, n, in, b_.count, b_.bytes) ||
+            !extent(m, n, sizeof(float), c_.count, c_.bytes) || !extent(m, k, sizeof(float), a_.count, host_a) ||
+            !extent(k, n, sizeof(float), b_.count, host_b))
+            invalid("matrix byte count overflows size_t");
+    }
+
+    ~Plan() {
+        if (kernel_) jr_kernel_release(kernel_);
+        if (!rt_) return;
+        for (void *p : {a_.ptr, b_.ptr, c_.ptr})
+            if (p) jr_free(rt_, p);
+        jr_destroy(rt_);
+    }
+
+    // Device context, buffers and the compiled GEMM.
+    void open() {
+        const int visible = jr_device_count();
+        if (device_ >= visible) jade::raise(kInvalid, "device %d outside detected count %d", device_, visible);
+        via_runtime([&](char *e, size_t c) { return jr_create(device_, &rt_, e, c); });
+        for (Matrix *mat : {&a_, &b_, &c_})
+            via_runtime([&](char *e, size_t c) { return jr_alloc(rt_, mat->bytes, &mat->ptr, e, c); });
+        const std::string spec = "{\"op\":\"gemm\",\"m\":" + std::to_string(m_) + ",\"n\":" + std::to_string(n_) +
+                                 ",\"k\":" + std::to_string(k_) + ",\"tiled\":true" +
+                                 (fp16_ ? ",\"dtype\":\"fp16\",\"out_dtype\":\"fp32\"}" : "}");
+        via_runtime([&](char *e, size_t c) { return jr_compile(rt_, spec.c_str(), &kernel_, e, c); });
+        if (fp16_) {
+            try {
+                half_a_.resize(a_.count);
+                half_b_.resize(b_.count);
+            } catch (const std::bad_alloc &) {
+                throw jade::Fault{kAllocation, "FP16 staging allocation failed"};
+            }
+        }
+    }
+
+    bool accepts_inputs(size_t a_len, size_t b_len) const { return a_len == a_.count && b_len == b_.count; }
+    bool accepts_output(size_t c_len) const { return c_len == c_.count; }
+
+    void upload(const float *a, const float *b) {
+        uploaded_ = computed_ = false;
+        const void *src[2] = {a, b};
+        if (fp16_) {  // round to nearest even, as the provider's fp16 conversion
+            for (size_t i = 0; i < a_.count; ++i) half_a_[i] = __half_as_ushort(__float2half_rn(a[i]));
+            for (size_t i = 0; i < b_.count; ++i) half_b_[i] = __half_as_ushort(__float2half_rn(b[i]));
+            src[0] = half_a_.data();
+            src[1] = half_b_.data();
+        }
+        via_runtime([&](char *e, size_t c) { return jr_upload(rt_, a_.ptr, src[0], a_.bytes, e, c); });
+        via_runtime([&](char *e, size_t c) { return jr_upload(rt_, b_.ptr, src[1], b_.bytes, e, c); });
+        uploaded_ = true;
+    }
+
+    double run(uint32_t iterations) {
+        computed_ = false;
+        if (!uploaded_) invalid("upload A/B before running");
+        void *buffers[3] = {a_.ptr, b_.ptr, c_.ptr};
+        const jr_dispatch job{kernel_, buffers, 3};
+        double ms = 0;
+        via_runtime([&](char *e, size_t c) { return jr_execute2(rt_, &job, 1, iterations, 0, &ms, nullptr, e, c); });
+        if (!std::isfinite(ms) || ms < 0) throw jade::Fault{kRuntime, "invalid GPU event duration"};
+        computed_ = true;
+        return ms;
+    }
+
+    void download(float *out) {
+        if (!computed_) invalid("run successfully before downloading C");
+        via_runtime([&](char *e, size_t c) { return jr_download(rt_, c_.ptr, out, c_.bytes, e, c); });
+    }
+
+    // "device=.. name=.. memory_bytes=.. multiprocessors=.. runtime_api=..
+    // driver_api=.. blas_api=0 precision=.. kernel=.."
+    void describe(char *out, size_t out_cap) const {
+        cudaError_t st = cudaSetDevice(device_);
+        if (st != cudaSuccess) jade::raise(kRuntime, "cudaSetDevice: %s", cudaGetErrorString(st));
+        cudaDeviceProp prop{};
+        st = cudaGetDeviceProperties(&prop, device_);
+        if (st != cudaSuccess) jade::raise(kRuntime, "cudaGetDeviceProperties: %s", cudaGetErrorString(st));
+        int runtime = 0, driver = 0;
+        if (cudaRuntimeGetVersion(&runtime) != cudaSuccess || cudaDriverGetVersion(&driver) != cudaSuccess)
+            throw jade::Fault{kRuntime, "CUDA version query failed"};
+        const int n = std::snprintf(out, out_cap,
+                                    "device=%d name=%.255s memory_bytes=%llu multiprocessors=%d runtime_api=%d driver_api=%d "
+                                    "blas_api=0 precision=%s kernel=%s",
+                                    device_, prop.name, static_cast<unsigned long long>(prop.totalGlobalMem),
+                                    prop.multiProcessorCount, runtime, driver, fp16_ ? "fp16_inputs_fp32_accum_output" : "fp32",
+                                    kernel_impl().c_str());
+        if (n < 0 || static_cast<size_t>(n) >= out_cap) {
+            out[out_cap - 1] = '\0';
+            invalid("device info output buffer too small");
+        }
+    }
+
+  private:
+    struct Matrix {
+        size_t count = 0, bytes = 0;
+        void *ptr = nullptr;
+    };
+
+    // The implementation name the runtime reports for the compiled GEMM.
+    std::string kernel_impl() const {
+        char info[2048];
+        if (jr_kernel_info(kernel_, info, sizeof info, nullptr, 0) != JR_OK) return "unknown";
+        const std::string text(info), key = "\"impl\":\"";
+        const size_t at = text.find(key);
+        if (at == std::string::npos) return "unknown";
+        const size_t from = at + key.size();
+        return text.substr(from, text.find('"', from) - from);
+    }
+
+    uint32_t m_, n_, k_;
+    int device_;
+    bool fp16_;
+    Matrix a_, b_, c_;
+    void *rt_ = nullptr;
+    jr_kernel *kernel_ = nullptr;
+    std::vector<uint16_t> half_a_, half_b_;
+    bool uploaded_ = false, computed_ = false;
 };
 
-void clear_error(char *err, size_t cap) {
-    if (err && cap) err[0] = '\0';
-}
-
-int fail(int code, char *err, size_t cap, const char *format, ...) {
-    if (err && cap) {
-        va_list args;
-        va_start(args, format);
-        std::vsnprintf(err, cap, format, args);
-        va_end(args);
-        err[cap - 1] = '\0';
-    }
-    return code;
-}
-
-// jr_* codes (1 invalid, 2 CUDA, 3 out of memory, 4 device timeout) to this
-// ABI's (1 invalid, 2 runtime, 4 allocation); the message is already in err.
-int map_code(int rc) {
-    switch (rc) {
-        case 0: return 0;
-        case JR_EINVAL: return 1;
-        case JR_ENOMEM: return 4;
-        default: return 2;
-    }
-}
-
-bool matrix_size(uint32_t x, uint32_t y, size_t element_size, size_t &count, size_t &bytes) {
-    const auto maximum = std::numeric_limits<size_t>::max();
-    if (!x || !y || static_cast<size_t>(x) > maximum / y) return false;
-    count = static_cast<size_t>(x) * y;
-    if (count > maximum / element_size) return false;
-    bytes = count * element_size;
-    return true;
-}
-
-void cleanup(Plan *p) {
-    if (!p) return;
-    if (p->kernel) jr_kernel_release(p->kernel);
-    if (p->rt) {
-        if (p->a) jr_free(p->rt, p->a);
-        if (p->b) jr_free(p->rt, p->b);
-        if (p->c) jr_free(p->rt, p->c);
-        jr_destroy(p->rt);
-    }
-    delete p;
-}
-
-std::string gemm_spec(const Plan &p) {
-    std::string s = "{\"op\":\"gemm\",\"m\":" + std::to_string(p.m) + ",\"n\":" + std::to_string(p.n) +
-                    ",\"k\":" + std::to_string(p.k) + ",\"tiled\":true";
-    if (p.precision) s += ",\"dtype\":\"fp16\",\"out_dtype\":\"fp32\"";
-    return s + "}";
+// c_entry with this ABI's allocation code for host allocation failures.
+template <class Body>
+int plan_entry(char *err, size_t cap, Body &&body) noexcept {
+    return jade::c_entry(err, cap, [&] {
+        try {
+            body();
+        } catch (const std::bad_alloc &) {
+            throw jade::Fault{kAllocation, "context allocation failed"};
+        }
+    });
 }
 
 }  // namespace
@@ -93,134 +185,51 @@ extern "C" JC_API uint32_t jade_corex_abi_version(void) { return 1; }
 
 extern "C" JC_API int jade_corex_create(uint32_t m, uint32_t n, uint32_t k, int device, uint32_t precision, void **out,
                                         char *err, size_t cap) {
-    clear_error(err, cap);
-    if (!out) return fail(1, err, cap, "null output handle");
-    *out = nullptr;
-    if (!m || !n || !k || m > INT_MAX || n > INT_MAX || k > INT_MAX || device < 0 || precision > 1)
-        return fail(1, err, cap, "dimensions must be 1..INT_MAX; device >= 0; precision 0 or 1");
-    Plan *p = new (std::nothrow) Plan();
-    if (!p) return fail(4, err, cap, "context allocation failed");
-    p->m = m;
-    p->n = n;
-    p->k = k;
-    p->device = device;
-    p->precision = precision;
-    const size_t input_size = precision ? sizeof(uint16_t) : sizeof(float);
-    if (!matrix_size(m, k, input_size, p->a_len, p->a_bytes) || !matrix_size(k, n, input_size, p->b_len, p->b_bytes) ||
-        !matrix_size(m, n, sizeof(float), p->c_len, p->c_bytes) ||
-        p->a_len > std::numeric_limits<size_t>::max() / sizeof(float) ||
-        p->b_len > std::numeric_limits<size_t>::max() / sizeof(float)) {
-        delete p;
-        return fail(1, err, cap, "matrix byte count overflows size_t");
-    }
-    const auto initialize = [&]() -> int {
-        const int count = jr_device_count();
-        if (count < 0) return fail(2, err, cap, "cudaGetDeviceCount failed");
-        if (device >= count) return fail(1, err, cap, "device %d outside detected count %d", device, count);
-        int rc = jr_create(device, &p->rt, err, cap);
-        if (rc) return map_code(rc);
-        if ((rc = jr_alloc(p->rt, p->a_bytes, &p->a, err, cap)) || (rc = jr_alloc(p->rt, p->b_bytes, &p->b, err, cap)) ||
-            (rc = jr_alloc(p->rt, p->c_bytes, &p->c, err, cap)))
-            return map_code(rc);
-        if ((rc = jr_compile(p->rt, gemm_spec(*p).c_str(), &p->kernel, err, cap))) return map_code(rc);
-        if (precision) {
-            try {
-                p->host_a.resize(p->a_len);
-                p->host_b.resize(p->b_len);
-            } catch (...) {
-                return fail(4, err, cap, "FP16 staging allocation failed");
-            }
-        }
-        return 0;
-    };
-    const int rc = initialize();
-    if (rc) {
-        cleanup(p);
-        return rc;
-    }
-    *out = p;
-    return 0;
+    return plan_entry(err, cap, [&] {
+        if (!out) invalid("null output handle");
+        *out = nullptr;
+        const bool dims_ok = m && n && k && m <= INT_MAX && n <= INT_MAX && k <= INT_MAX;
+        if (!dims_ok || device < 0 || precision > 1) invalid("dimensions must be 1..INT_MAX; device >= 0; precision 0 or 1");
+        auto plan = std::make_unique<Plan>(m, n, k, device, precision);
+        plan->open();
+        *out = plan.release();
+    });
 }
 
 extern "C" JC_API int jade_corex_upload(void *handle, const float *a, size_t a_len, const float *b, size_t b_len,
                                         char *err, size_t cap) {
-    clear_error(err, cap);
-    auto *p = static_cast<Plan *>(handle);
-    if (!p || !a || !b || a_len != p->a_len || b_len != p->b_len)
-        return fail(1, err, cap, "upload requires non-null buffers and exact A/B element counts");
-    p->uploaded = false;
-    p->computed = false;
-    const void *src_a = a, *src_b = b;
-    if (p->precision) {
-        for (size_t i = 0; i < a_len; ++i) p->host_a[i] = __half_as_ushort(__float2half_rn(a[i]));
-        for (size_t i = 0; i < b_len; ++i) p->host_b[i] = __half_as_ushort(__float2half_rn(b[i]));
-        src_a = p->host_a.data();
-        src_b = p->host_b.data();
-    }
-    int rc = jr_upload(p->rt, p->a, src_a, p->a_bytes, err, cap);
-    if (!rc) rc = jr_upload(p->rt, p->b, src_b, p->b_bytes, err, cap);
-    if (rc) return map_code(rc);
-    p->uploaded = true;
-    return 0;
+    return plan_entry(err, cap, [&] {
+        auto *plan = static_cast<Plan *>(handle);
+        if (!plan || !a || !b || !plan->accepts_inputs(a_len, b_len))
+            invalid("upload requires non-null buffers and exact A/B element counts");
+        plan->upload(a, b);
+    });
 }
 
 extern "C" JC_API int jade_corex_run(void *handle, uint32_t iterations, double *elapsed_ms, char *err, size_t cap) {
-    clear_error(err, cap);
     if (elapsed_ms) *elapsed_ms = 0;
-    auto *p = static_cast<Plan *>(handle);
-    if (!p || !iterations || !elapsed_ms) return fail(1, err, cap, "run requires context, iterations > 0 and elapsed output");
-    p->computed = false;
-    if (!p->uploaded) return fail(1, err, cap, "upload A/B before running");
-    void *buffers[3] = {p->a, p->b, p->c};
-    const jr_dispatch job{p->kernel, buffers, 3};
-    double ms = 0;
-    const int rc = jr_execute2(p->rt, &job, 1, iterations, 0, &ms, nullptr, err, cap);
-    if (rc) return map_code(rc);
-    if (!std::isfinite(ms) || ms < 0) return fail(2, err, cap, "invalid GPU event duration");
-    *elapsed_ms = ms;
-    p->computed = true;
-    return 0;
+    return plan_entry(err, cap, [&] {
+        auto *plan = static_cast<Plan *>(handle);
+        if (!plan || !iterations || !elapsed_ms) invalid("run requires context, iterations > 0 and elapsed output");
+        *elapsed_ms = plan->run(iterations);
+    });
 }
 
 extern "C" JC_API int jade_corex_download(void *handle, float *out, size_t out_len, char *err, size_t cap) {
-    clear_error(err, cap);
-    auto *p = static_cast<Plan *>(handle);
-    if (!p || !out || out_len != p->c_len) return fail(1, err, cap, "download requires exact C element count");
-    if (!p->computed) return fail(1, err, cap, "run successfully before downloading C");
-    return map_code(jr_download(p->rt, p->c, out, p->c_bytes, err, cap));
+    return plan_entry(err, cap, [&] {
+        auto *plan = static_cast<Plan *>(handle);
+        if (!plan || !out || !plan->accepts_output(out_len)) invalid("download requires exact C element count");
+        plan->download(out);
+    });
 }
 
 extern "C" JC_API int jade_corex_device_info(void *handle, char *out, size_t out_cap, char *err, size_t cap) {
-    clear_error(err, cap);
     if (out && out_cap) out[0] = '\0';
-    auto *p = static_cast<Plan *>(handle);
-    if (!p || !out || !out_cap) return fail(1, err, cap, "device info requires context and output buffer");
-    auto status = cudaSetDevice(p->device);
-    if (status != cudaSuccess) return fail(2, err, cap, "cudaSetDevice: %s", cudaGetErrorString(status));
-    cudaDeviceProp prop{};
-    status = cudaGetDeviceProperties(&prop, p->device);
-    if (status != cudaSuccess) return fail(2, err, cap, "cudaGetDeviceProperties: %s", cudaGetErrorString(status));
-    int runtime = 0, driver = 0;
-    if (cudaRuntimeGetVersion(&runtime) != cudaSuccess || cudaDriverGetVersion(&driver) != cudaSuccess)
-        return fail(2, err, cap, "CUDA version query failed");
-    char kinfo[1024];
-    std::string impl = "unknown";
-    if (jr_kernel_info(p->kernel, kinfo, sizeof kinfo, nullptr, 0) == 0) {
-        const std::string s(kinfo);
-        const auto at = s.find("\"impl\":\"");
-        if (at != std::string::npos) impl = s.substr(at + 8, s.find('"', at + 8) - (at + 8));
-    }
-    const int needed = std::snprintf(
-        out, out_cap,
-        "device=%d name=%.255s memory_bytes=%llu multiprocessors=%d runtime_api=%d driver_api=%d blas_api=0 precision=%s "
-        "kernel=%s",
-        p->device, prop.name, static_cast<unsigned long long>(prop.totalGlobalMem), prop.multiProcessorCount, runtime,
-        driver, p->precision ? "fp16_inputs_fp32_accum_output" : "fp32", impl.c_str());
-    if (needed < 0 || static_cast<size_t>(needed) >= out_cap) {
-        out[out_cap - 1] = '\0';
-        return fail(1, err, cap, "device info output buffer too small");
-    }
-    return 0;
+    return plan_entry(err, cap, [&] {
+        auto *plan = static_cast<Plan *>(handle);
+        if (!plan || !out || !out_cap) invalid("device info requires context and output buffer");
+        plan->describe(out, out_cap);
+    });
 }
 
-extern "C" JC_API void jade_corex_destroy(void *handle) { cleanup(static_cast<Plan *>(handle)); }
+extern "C" JC_API void jade_corex_destroy(void *handle) { delete static_cast<Plan *>(handle); }

@@ -397,19 +397,26 @@ LaunchFn pick_epilogue(Context *ctx, const Spec &s) {
 }
 
 // FP32 [rows, cols] -> [cols, rows] through 32x32 shared-memory tiles.
+// out[c][r] = in[r][c] for a rows x cols FP32 matrix, through 32 x 33 shared
+// tiles. Row blocks are grid-strided, so any row count fits the 65535 limit of
+// gridDim.y (launch with transpose_grid).
 __global__ void transpose_f32(const float *__restrict__ in, float *__restrict__ out, int rows, int cols) {
     __shared__ float tile[32][33];
-    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int r = r0 + i, c = c0 + threadIdx.x;
-        if (r < rows && c < cols) tile[i][threadIdx.x] = in[(size_t)r * cols + c];
-    }
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int c = c0 + i, r = r0 + threadIdx.x;
-        if (r < rows && c < cols) out[(size_t)c * rows + r] = tile[threadIdx.x][i];
+    const int c0 = blockIdx.x * 32;
+    for (int r0 = blockIdx.y * 32; r0 < rows; r0 += gridDim.y * 32) {
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int r = r0 + i, c = c0 + threadIdx.x;
+            if (r < rows && c < cols) tile[i][threadIdx.x] = in[(size_t)r * cols + c];
+        }
+        __syncthreads();
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int c = c0 + i, r = r0 + threadIdx.x;
+            if (r < rows && c < cols) out[(size_t)c * rows + r] = tile[threadIdx.x][i];
+        }
+        __syncthreads();
     }
 }
+inline dim3 transpose_grid(int rows, int cols) { return dim3((cols + 31) / 32, std::min((rows + 31) / 32, 65535)); }
 
 // Device workspace owned by a compiled kernel, released with it.
 struct Workspace {
@@ -458,7 +465,7 @@ LaunchFn make_gemm_tc(Context *ctx, const Spec &s, std::string &impl) {
                 const int K = (int)s.k, N = (int)s.n;
                 const bool extra = s.row_scale || s.epilogue == "residual";
                 return [=](cudaStream_t st, void **b) {
-                    transpose_f32<<<dim3((N + 31) / 32, (K + 31) / 32), dim3(32, 8), 0, st>>>((const float *)b[0 + 1], (float *)ws->ptr, K, N);
+                    transpose_f32<<<transpose_grid(K, N), dim3(32, 8), 0, st>>>((const float *)b[0 + 1], (float *)ws->ptr, K, N);
                     void *nb[5] = {b[0], ws->ptr, b[2], extra ? b[3] : nullptr, extra ? b[4] : nullptr};
                     return inner(st, nb);
                 };
@@ -528,6 +535,8 @@ extern "C" JR_API int jr_gemm_tf32_kn_noalloc(const float *a, const float *b, fl
     }
     if (k % 4 || (reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) % 16)
         return noalloc_fail(1, err, cap, "TMA needs K to be a multiple of 4 and 16-byte aligned A and B");
+    if (reinterpret_cast<uintptr_t>(out) % 16)  // the epilogue stores 16-byte vectors of a row
+        return noalloc_fail(1, err, cap, "out must be 16-byte aligned");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return noalloc_fail(2, err, cap, "cudaGetDevice failed");
     auto kernel = gemm_tc_kernel<4, 2, false, float, kEpiNone, false>;
@@ -567,15 +576,21 @@ extern "C" JR_API int jr_gemm_tf32_kn_noalloc(const float *a, const float *b, fl
     args.err = d->err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // B [K,N] -> scratch [N,K]: the whole K*N region is rewritten, nothing needs clearing.
-    transpose_f32<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, st>>>(b, d->scratch, (int)k, (int)n);
+    transpose_f32<<<transpose_grid((int)k, (int)n), dim3(32, 8), 0, st>>>(b, d->scratch, (int)k, (int)n);
     kernel<<<std::min(args.num_tiles, d->sm_count), kThreads, kSmemBytes, st>>>(ma, mb, args);
     cudaError_t status = cudaGetLastError();
     if (status == cudaSuccess) status = cudaStreamSynchronize(st);
     if (status != cudaSuccess) return noalloc_fail(2, err, cap, cudaGetErrorString(status));
+    // The error word is read on the caller's stream (no legacy-stream copy, so no
+    // implicit synchronisation with other streams of the device).
     int code = 0;
-    if (cudaMemcpy(&code, d->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return noalloc_fail(2, err, cap, "error word read failed");
+    status = cudaMemcpyAsync(&code, d->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (status == cudaSuccess) status = cudaStreamSynchronize(st);
+    if (status != cudaSuccess) return noalloc_fail(2, err, cap, "error word read failed");
     if (code) {
-        cudaMemset(d->err, 0, sizeof(int));  // the word must start at zero for the next call
+        // the word must start at zero for the next call
+        if (cudaMemsetAsync(d->err, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+            return noalloc_fail(2, err, cap, "error word reset failed");
         return noalloc_fail(4, err, cap, "device-side bounded wait expired in the TF32 GEMM");
     }
     return 0;

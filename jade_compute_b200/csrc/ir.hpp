@@ -105,6 +105,9 @@ std::string metal_source(const Spec &s);
 // sm_100a lowering of an elementwise expression: a vectorised grid-stride kernel
 // named jade_elementwise(const float* input0.., float* out, unsigned long long n).
 std::string cuda_elementwise_source(const Spec &s);
+// Text of the "cuda" emit target (jr_spec_emit): an sm_100a translation unit for
+// the spec with the ABI-1 launcher jade_generated_launch(stream, buffers).
+std::string cuda_source(const Spec &s);
 std::string expr_cuda_code(const Expr &e, const std::vector<std::string> &names);
 
 Json binding_to_json(const Binding &b);

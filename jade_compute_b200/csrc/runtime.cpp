@@ -1,101 +1,37 @@
 // C ABI of the B200 runtime (include/jade_runtime.h).
 //
-// ABI 1 follows native/jade_runtime_corex.cpp:81-224 exactly: one device, one
-// non-blocking stream, two timing events, zero-filled allocations, synchronous
-// exact transfers, and an ordered execute that validates every job before it
-// submits any and brackets the whole repeats x jobs sequence with one event pair.
-// ABI 2 adds a buffer registry (so ownership, exact sizes and write aliasing are
-// checked natively, as src/runtime/corex.rs:557-569 does in the caller), the
-// JSON KernelSpec front end, built-in sm_100a kernels, per-job timing, CUDA-graph
-// replay, and collectives.
+// A context is one device with one non-blocking stream, a timing-event pair, a
+// mapped error word written by the kernels' bounded waits, and a registry of
+// every buffer it handed out. ABI 1 (jr_version() == 1) is the reference
+// bridge's surface over that context: raw launcher jobs run in order between the
+// event pair. ABI 2 builds on the same pieces: the JSON KernelSpec front end,
+// built-in sm_100a kernels, registry checks of every job before any launch (as
+// src/runtime/corex.rs:557-569 does in the caller), per-job timing, CUDA-graph
+// replay, dependency-scheduled transfer streams and collectives.
+//
+// Every exported function is a jade::c_entry body (cabi.hpp): failures are
+// thrown as jade::Fault and turned into the return code and message there.
 #include <cuda.h>
 #include <cuda_runtime.h>
-#include <dlfcn.h>
 
 #include <algorithm>
 #include <chrono>
-#include <map>
 #include <cmath>
-#include <cstdarg>
-#include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <new>
+#include <map>
+#include <memory>
 #include <thread>
 
 #include "../../include/jade_runtime.h"
+#include "cabi.hpp"
 #include "internal.hpp"
 
+using jade::check_cuda;
 using jade::Context;
-
-namespace {
-
-int fail(int code, char *err, size_t cap, const char *format, ...) {
-    if (err && cap) {
-        va_list args;
-        va_start(args, format);
-        std::vsnprintf(err, cap, format, args);
-        va_end(args);
-        err[cap - 1] = '\0';
-    }
-    return code;
-}
-void clear(char *err, size_t cap) {
-    if (err && cap) err[0] = '\0';
-}
-int cuda_fail(cudaError_t status, char *err, size_t cap, const char *operation) {
-    return fail(JR_ECUDA, err, cap, "%s: %s (%d)", operation, cudaGetErrorString(status), static_cast<int>(status));
-}
-int select(Context *ctx, char *err, size_t cap) {
-    if (!ctx) return fail(JR_EINVAL, err, cap, "null runtime context");
-    const auto status = cudaSetDevice(ctx->device);
-    return status == cudaSuccess ? 0 : cuda_fail(status, err, cap, "cudaSetDevice");
-}
-void destroy(Context *ctx) {
-    if (!ctx) return;
-    cudaSetDevice(ctx->device);
-    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    jade::comm_destroy(ctx);
-    jade::cublas_destroy(ctx);
-    jade::rtc_destroy(ctx);
-    for (auto &a : ctx->allocations) {
-        if (a.second.host) cudaFreeHost(reinterpret_cast<void *>(a.first));
-        else cudaFree(reinterpret_cast<void *>(a.first));
-    }
-    for (auto e : ctx->job_events) cudaEventDestroy(e);
-    for (auto e : ctx->dep_events) cudaEventDestroy(e);
-    if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
-    if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
-    if (ctx->err_host) cudaFreeHost(ctx->err_host);
-    if (ctx->start) cudaEventDestroy(ctx->start);
-    if (ctx->stop) cudaEventDestroy(ctx->stop);
-    if (ctx->stream) cudaStreamDestroy(ctx->stream);
-    delete ctx;
-}
-int copy_out(const std::string &s, char *out, size_t out_cap, char *err, size_t cap) {
-    if (!out || !out_cap) return fail(JR_EINVAL, err, cap, "missing output buffer");
-    if (s.size() + 1 > out_cap) {
-        out[0] = '\0';
-        return fail(JR_EINVAL, err, cap, "output buffer too small (%zu bytes needed)", s.size() + 1);
-    }
-    memcpy(out, s.c_str(), s.size() + 1);
-    return 0;
-}
-
-// Reads and clears the device error word written by bounded waits.
-int check_device_error(Context *ctx, char *err, size_t cap) {
-    if (!ctx->err_host) return 0;
-    const int code = *reinterpret_cast<volatile int *>(ctx->err_host);
-    if (!code) return 0;
-    *reinterpret_cast<volatile int *>(ctx->err_host) = 0;
-    static const char *what[] = {"", "MMA wait for a TMA stage", "producer wait for a free stage", "epilogue wait for an accumulator",
-                                 "MMA wait for a drained accumulator", "softmax wait for scores", "MMA wait for probabilities",
-                                 "correction wait for P.V", "exit wait for copies in flight", "launch geometry mismatch"};
-    return fail(JR_ETIMEOUT, err, cap, "device-side bounded wait expired: %s (code %d)", code > 0 && code < 10 ? what[code] : "unknown",
-                code);
-}
-
-}  // namespace
+using jade::Fault;
+using jade::raise;
+using jade::require;
 
 namespace jade {
 void *driver_entry(const char *name) {
@@ -105,12 +41,147 @@ void *driver_entry(const char *name) {
         return nullptr;
     return fn;
 }
+void comm_poll_abort(Context *ctx);  // comm.cpp: throws JR_ETIMEOUT on an asynchronous NCCL error
 }  // namespace jade
 
-// ============================================================== ABI 1
 namespace {
-// 16-bit attention kernel choice: JADE_ATTENTION_KERNEL=pair or two_tile forces one
-// (read when a kernel is compiled); otherwise the measured rule of
+
+// ------------------------------------------------------------ context plumbing
+
+// The context behind a caller's handle, with its device made current.
+Context &enter(void *handle) {
+    auto *ctx = static_cast<Context *>(handle);
+    require(ctx != nullptr, "null runtime context");
+    check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice");
+    return *ctx;
+}
+
+// Teardown never reports: it runs from jr_destroy and from a failed jr_create.
+// Queued work finishes first, then the collective, libraries, registered
+// buffers, events and streams go, in that order.
+void teardown(Context *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    jade::comm_destroy(ctx);
+    jade::cublas_destroy(ctx);
+    jade::rtc_destroy(ctx);
+    for (const auto &entry : ctx->allocations) {
+        void *p = reinterpret_cast<void *>(entry.first);
+        if (entry.second.host) cudaFreeHost(p);
+        else cudaFree(p);
+    }
+    ctx->allocations.clear();
+    for (cudaEvent_t e : ctx->job_events) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->dep_events) cudaEventDestroy(e);
+    for (cudaEvent_t e : {ctx->start, ctx->stop})
+        if (e) cudaEventDestroy(e);
+    for (cudaStream_t s : {ctx->copy_in, ctx->copy_out, ctx->stream})
+        if (s) cudaStreamDestroy(s);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
+    delete ctx;
+}
+
+// A fresh context on `device`: its stream, timing events, mapped error word and
+// SM count. Throws with everything created so far released.
+Context *build_context(int device) {
+    std::unique_ptr<Context, void (*)(Context *)> ctx(new (std::nothrow) Context, teardown);
+    if (!ctx) raise(JR_ENOMEM, "runtime context allocation failed");
+    ctx->device = device;
+    check_cuda(cudaSetDevice(device), "cudaSetDevice");
+    cudaError_t st = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    for (cudaEvent_t *e : {&ctx->start, &ctx->stop})
+        if (st == cudaSuccess) st = cudaEventCreate(e);
+    if (st == cudaSuccess) st = cudaHostAlloc(reinterpret_cast<void **>(&ctx->err_host), 64, cudaHostAllocMapped);
+    if (st == cudaSuccess) st = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->err_dev), ctx->err_host, 0);
+    if (st == cudaSuccess) st = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    check_cuda(st, "create stream/timing events");
+    std::memset(ctx->err_host, 0, 64);
+    return ctx.release();
+}
+
+// Device memory registered with the context and zero-filled before it is
+// returned, so a buffer never exposes stale contents.
+void *device_buffer(Context &ctx, size_t bytes) {
+    void *p = nullptr;
+    const cudaError_t st = cudaMalloc(&p, bytes);
+    if (st != cudaSuccess) {
+        cudaGetLastError();
+        raise(st == cudaErrorMemoryAllocation ? JR_ENOMEM : JR_ECUDA, "cudaMalloc: %s (%d)", cudaGetErrorString(st), (int)st);
+    }
+    const cudaError_t zero = cudaMemsetAsync(p, 0, bytes, ctx.stream);
+    const cudaError_t done = cudaStreamSynchronize(ctx.stream);
+    if (zero != cudaSuccess || done != cudaSuccess) {
+        cudaFree(p);
+        check_cuda(zero != cudaSuccess ? zero : done, "initialize allocation");
+    }
+    ctx.allocations[reinterpret_cast<uintptr_t>(p)] = jade::Allocation{bytes, false};
+    return p;
+}
+
+// One blocking transfer on the context stream; `name` is "upload" or "download".
+void blocking_copy(Context &ctx, void *dst, const void *src, size_t bytes, cudaMemcpyKind kind, const char *name) {
+    const cudaError_t issued = cudaMemcpyAsync(dst, src, bytes, kind, ctx.stream);
+    const cudaError_t done = cudaStreamSynchronize(ctx.stream);
+    check_cuda(issued, name);
+    check_cuda(done, (std::string(name) + " synchronization").c_str());
+}
+
+// Reads and clears the error word the kernels' bounded waits write (first
+// expiry wins), as JR_ETIMEOUT naming the wait that gave up.
+void raise_device_wait_error(Context &ctx) {
+    if (!ctx.err_host) return;
+    volatile int *word = reinterpret_cast<volatile int *>(ctx.err_host);
+    const int code = *word;
+    if (!code) return;
+    *word = 0;
+    static const char *const site[] = {"",
+                                       "MMA wait for a TMA stage",
+                                       "producer wait for a free stage",
+                                       "epilogue wait for an accumulator",
+                                       "MMA wait for a drained accumulator",
+                                       "softmax wait for scores",
+                                       "MMA wait for probabilities",
+                                       "correction wait for P.V",
+                                       "exit wait for copies in flight",
+                                       "launch geometry mismatch"};
+    const bool known = code > 0 && code < (int)(sizeof site / sizeof site[0]);
+    raise(JR_ETIMEOUT, "device-side bounded wait expired: %s (code %d)", known ? site[code] : "unknown", code);
+}
+
+// Blocks until `ev` completes. With a collective in flight the wait polls NCCL's
+// asynchronous error state and gives up after the context's collective timeout,
+// aborting the communicator so that queued collectives return.
+void await_event(Context &ctx, cudaEvent_t ev, bool collective) {
+    if (!collective) {
+        check_cuda(cudaEventSynchronize(ev), "kernel synchronization");
+        return;
+    }
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(ctx.comm_timeout_ms);
+    for (;;) {
+        const cudaError_t st = cudaEventQuery(ev);
+        if (st == cudaSuccess) return;
+        if (st != cudaErrorNotReady) check_cuda(st, "kernel synchronization");
+        jade::comm_poll_abort(&ctx);
+        if (std::chrono::steady_clock::now() > deadline) {
+            jade::comm_destroy(&ctx);
+            cudaStreamSynchronize(ctx.stream);
+            raise(JR_ETIMEOUT, "collective did not complete within %u ms; communicator aborted", ctx.comm_timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// Milliseconds between the context's start and stop events, already completed.
+double bracket_ms(Context &ctx) {
+    float ms = 0;
+    check_cuda(cudaEventElapsedTime(&ms, ctx.start, ctx.stop), "event elapsed time");
+    if (!std::isfinite(ms) || ms < 0) raise(JR_ECUDA, "invalid GPU-event duration");
+    return ms;
+}
+
+// 16-bit attention kernel choice: JADE_ATTENTION_KERNEL=pair or two_tile forces
+// one (read when a kernel is compiled); otherwise the measured rule of
 // attention_prefers_pair decides.
 bool attention_use_pair(const jade::Spec &s, int sm_count) {
     const char *force = std::getenv("JADE_ATTENTION_KERNEL");
@@ -120,169 +191,110 @@ bool attention_use_pair(const jade::Spec &s, int sm_count) {
     if (s.dim != 128) throw jade::IrError("the pair attention kernel needs head dim 128");
     return true;
 }
+
 }  // namespace
 
+// ============================================================== ABI 1
 extern "C" uint32_t jr_version(void) { return 1; }
 
 extern "C" int jr_create(int device, void **out, char *err, size_t cap) {
-    clear(err, cap);
-    if (!out) return fail(JR_EINVAL, err, cap, "null output handle");
-    *out = nullptr;
-    if (device < 0) return fail(JR_EINVAL, err, cap, "negative device index");
-    int count = 0;
-    auto status = cudaGetDeviceCount(&count);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "cudaGetDeviceCount");
-    if (device >= count) return fail(JR_EINVAL, err, cap, "device %d outside device count %d", device, count);
-    auto *ctx = new (std::nothrow) Context;
-    if (!ctx) return fail(JR_ENOMEM, err, cap, "runtime context allocation failed");
-    ctx->device = device;
-    int rc = select(ctx, err, cap);
-    if (rc) {
-        destroy(ctx);
-        return rc;
-    }
-    status = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-    if (status == cudaSuccess) status = cudaEventCreate(&ctx->start);
-    if (status == cudaSuccess) status = cudaEventCreate(&ctx->stop);
-    if (status == cudaSuccess) status = cudaHostAlloc(reinterpret_cast<void **>(&ctx->err_host), 64, cudaHostAllocMapped);
-    if (status == cudaSuccess) status = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->err_dev), ctx->err_host, 0);
-    if (status == cudaSuccess) status = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
-    if (status != cudaSuccess) {
-        rc = cuda_fail(status, err, cap, "create stream/timing events");
-        destroy(ctx);
-        return rc;
-    }
-    memset(ctx->err_host, 0, 64);
-    *out = ctx;
-    return 0;
+    return jade::c_entry(err, cap, [&] {
+        require(out != nullptr, "null output handle");
+        *out = nullptr;
+        require(device >= 0, "negative device index");
+        int visible = 0;
+        check_cuda(cudaGetDeviceCount(&visible), "cudaGetDeviceCount");
+        if (device >= visible) raise(JR_EINVAL, "device %d outside device count %d", device, visible);
+        *out = build_context(device);
+    });
 }
 
-extern "C" void jr_destroy(void *ctx) { destroy(static_cast<Context *>(ctx)); }
+extern "C" void jr_destroy(void *ctx) { teardown(static_cast<Context *>(ctx)); }
 
 extern "C" int jr_info(void *handle, char *out, size_t out_cap, char *err, size_t cap) {
-    clear(err, cap);
     if (out && out_cap) out[0] = '\0';
-    if (!out || !out_cap) return fail(JR_EINVAL, err, cap, "missing device-info output");
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    cudaDeviceProp prop{};
-    auto status = cudaGetDeviceProperties(&prop, ctx->device);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "cudaGetDeviceProperties");
-    int runtime = 0, driver = 0;
-    status = cudaRuntimeGetVersion(&runtime);
-    if (status == cudaSuccess) status = cudaDriverGetVersion(&driver);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "runtime/driver version");
-    const int n = std::snprintf(out, out_cap, "device=%d name=%.255s memory_bytes=%llu runtime_api=%d driver_api=%d", ctx->device, prop.name,
-                                static_cast<unsigned long long>(prop.totalGlobalMem), runtime, driver);
-    if (n < 0 || static_cast<size_t>(n) >= out_cap) {
-        out[out_cap - 1] = '\0';
-        return fail(JR_EINVAL, err, cap, "device-info output too small");
-    }
-    return 0;
+    return jade::c_entry(err, cap, [&] {
+        require(out && out_cap, "missing device-info output");
+        Context &ctx = enter(handle);
+        cudaDeviceProp prop{};
+        check_cuda(cudaGetDeviceProperties(&prop, ctx.device), "cudaGetDeviceProperties");
+        int runtime = 0, driver = 0;
+        cudaError_t st = cudaRuntimeGetVersion(&runtime);
+        if (st == cudaSuccess) st = cudaDriverGetVersion(&driver);
+        check_cuda(st, "runtime/driver version");
+        const int n = std::snprintf(out, out_cap, "device=%d name=%.255s memory_bytes=%llu runtime_api=%d driver_api=%d", ctx.device,
+                                    prop.name, static_cast<unsigned long long>(prop.totalGlobalMem), runtime, driver);
+        if (n < 0 || static_cast<size_t>(n) >= out_cap) {
+            out[out_cap - 1] = '\0';
+            raise(JR_EINVAL, "device-info output too small");
+        }
+    });
 }
 
 extern "C" int jr_alloc(void *handle, size_t bytes, void **out, char *err, size_t cap) {
-    clear(err, cap);
-    if (!out) return fail(JR_EINVAL, err, cap, "null allocation output");
-    *out = nullptr;
-    if (!bytes) return fail(JR_EINVAL, err, cap, "allocation must be nonempty");
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    auto status = cudaMalloc(out, bytes);
-    if (status != cudaSuccess) {
-        cudaGetLastError();
+    return jade::c_entry(err, cap, [&] {
+        require(out != nullptr, "null allocation output");
         *out = nullptr;
-        return fail(status == cudaErrorMemoryAllocation ? JR_ENOMEM : JR_ECUDA, err, cap, "cudaMalloc: %s (%d)", cudaGetErrorString(status),
-                    (int)status);
-    }
-    // Public allocations contain defined zeros, even before the first upload.
-    status = cudaMemsetAsync(*out, 0, bytes, ctx->stream);
-    const auto sync = cudaStreamSynchronize(ctx->stream);
-    if (status != cudaSuccess || sync != cudaSuccess) {
-        cudaFree(*out);
-        *out = nullptr;
-        return cuda_fail(status != cudaSuccess ? status : sync, err, cap, "initialize allocation");
-    }
-    ctx->allocations[reinterpret_cast<uintptr_t>(*out)] = jade::Allocation{bytes, false};
-    return 0;
+        require(bytes != 0, "allocation must be nonempty");
+        *out = device_buffer(enter(handle), bytes);
+    });
 }
 
 extern "C" void jr_free(void *handle, void *ptr) {
-    if (!handle || !ptr) return;
     auto *ctx = static_cast<Context *>(handle);
-    if (cudaSetDevice(ctx->device) != cudaSuccess) return;
+    if (!ctx || !ptr || cudaSetDevice(ctx->device) != cudaSuccess) return;
     cudaStreamSynchronize(ctx->stream);
-    auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(ptr));
+    const auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(ptr));
     if (it != ctx->allocations.end()) {
-        if (it->second.host) return;  // host buffers are released by jr_host_free
+        if (it->second.host) return;  // pinned host buffers go through jr_host_free
         ctx->allocations.erase(it);
     }
     cudaFree(ptr);
 }
 
 extern "C" int jr_upload(void *handle, void *device_ptr, const void *host_ptr, size_t bytes, char *err, size_t cap) {
-    clear(err, cap);
-    if (!device_ptr || !host_ptr || !bytes) return fail(JR_EINVAL, err, cap, "invalid upload buffers/size");
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    const auto status = cudaMemcpyAsync(device_ptr, host_ptr, bytes, cudaMemcpyHostToDevice, ctx->stream);
-    const auto sync = cudaStreamSynchronize(ctx->stream);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "upload");
-    return sync == cudaSuccess ? 0 : cuda_fail(sync, err, cap, "upload synchronization");
+    return jade::c_entry(err, cap, [&] {
+        require(device_ptr && host_ptr && bytes, "invalid upload buffers/size");
+        blocking_copy(enter(handle), device_ptr, host_ptr, bytes, cudaMemcpyHostToDevice, "upload");
+    });
 }
 
 extern "C" int jr_download(void *handle, const void *device_ptr, void *host_ptr, size_t bytes, char *err, size_t cap) {
-    clear(err, cap);
-    if (!device_ptr || !host_ptr || !bytes) return fail(JR_EINVAL, err, cap, "invalid download buffers/size");
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    const auto status = cudaMemcpyAsync(host_ptr, device_ptr, bytes, cudaMemcpyDeviceToHost, ctx->stream);
-    const auto sync = cudaStreamSynchronize(ctx->stream);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "download");
-    return sync == cudaSuccess ? 0 : cuda_fail(sync, err, cap, "download synchronization");
+    return jade::c_entry(err, cap, [&] {
+        require(device_ptr && host_ptr && bytes, "invalid download buffers/size");
+        blocking_copy(enter(handle), host_ptr, device_ptr, bytes, cudaMemcpyDeviceToHost, "download");
+    });
 }
 
 extern "C" int jr_execute(void *handle, const jr_job *jobs, size_t job_count, uint32_t repeats, double *gpu_ms, char *err, size_t cap) {
-    clear(err, cap);
     if (gpu_ms) *gpu_ms = 0;
-    if (!jobs || !job_count || !repeats || !gpu_ms) return fail(JR_EINVAL, err, cap, "empty dispatch sequence or missing timing output");
-    // Validate every job before any work is submitted.
-    for (size_t j = 0; j < job_count; ++j) {
-        if (!jobs[j].launch || !jobs[j].buffers || !jobs[j].buffer_count) return fail(JR_EINVAL, err, cap, "invalid job %zu", j);
-        for (size_t b = 0; b < jobs[j].buffer_count; ++b)
-            if (!jobs[j].buffers[b]) return fail(JR_EINVAL, err, cap, "null buffer in job %zu", j);
-    }
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    auto status = cudaEventRecord(ctx->start, ctx->stream);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "record start event");
-    for (uint32_t repeat = 0; repeat < repeats; ++repeat) {
+    return jade::c_entry(err, cap, [&] {
+        require(jobs && job_count && repeats && gpu_ms, "empty dispatch sequence or missing timing output");
+        // The whole sequence is checked before the device sees any of it.
         for (size_t j = 0; j < job_count; ++j) {
-            status = static_cast<cudaError_t>(jobs[j].launch(static_cast<void *>(ctx->stream), jobs[j].buffers));
-            if (status != cudaSuccess) {
-                cudaStreamSynchronize(ctx->stream);
-                return cuda_fail(status, err, cap, "generated kernel launch");
+            const jr_job &job = jobs[j];
+            if (!job.launch || !job.buffers || !job.buffer_count) raise(JR_EINVAL, "invalid job %zu", j);
+            if (std::find(job.buffers, job.buffers + job.buffer_count, nullptr) != job.buffers + job.buffer_count)
+                raise(JR_EINVAL, "null buffer in job %zu", j);
+        }
+        Context &ctx = enter(handle);
+        check_cuda(cudaEventRecord(ctx.start, ctx.stream), "record start event");
+        for (uint64_t launch = 0, total = (uint64_t)repeats * job_count; launch < total; ++launch) {
+            const jr_job &job = jobs[launch % job_count];
+            const auto st = static_cast<cudaError_t>(job.launch(static_cast<void *>(ctx.stream), job.buffers));
+            if (st != cudaSuccess) {
+                cudaStreamSynchronize(ctx.stream);
+                check_cuda(st, "generated kernel launch");
             }
         }
-    }
-    status = cudaEventRecord(ctx->stop, ctx->stream);
-    if (status != cudaSuccess) {
-        cudaStreamSynchronize(ctx->stream);
-        return cuda_fail(status, err, cap, "record stop event");
-    }
-    status = cudaEventSynchronize(ctx->stop);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "kernel synchronization");
-    float elapsed = 0;
-    status = cudaEventElapsedTime(&elapsed, ctx->start, ctx->stop);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "event elapsed time");
-    if (!std::isfinite(elapsed) || elapsed < 0) return fail(JR_ECUDA, err, cap, "invalid GPU-event duration");
-    *gpu_ms = static_cast<double>(elapsed);
-    return 0;
+        const cudaError_t stop = cudaEventRecord(ctx.stop, ctx.stream);
+        if (stop != cudaSuccess) {
+            cudaStreamSynchronize(ctx.stream);
+            check_cuda(stop, "record stop event");
+        }
+        check_cuda(cudaEventSynchronize(ctx.stop), "kernel synchronization");
+        *gpu_ms = bracket_ms(ctx);
+    });
 }
 
 // ============================================================== ABI 2
@@ -297,432 +309,405 @@ extern "C" int jr_device_count(void) {
     return n;
 }
 
-#define IR_GUARD(body)                                                  \
-    try {                                                               \
-        body                                                            \
-    } catch (const std::exception &e) {                                 \
-        return fail(JR_EINVAL, err, cap, "%s", e.what());               \
-    }
-
+// KernelSpec front end: parse/validate errors (jade::IrError) become JR_EINVAL
+// with the reference's message text.
 extern "C" int jr_spec_validate(const char *spec_json, char *err, size_t cap) {
-    clear(err, cap);
-    if (!spec_json) return fail(JR_EINVAL, err, cap, "null spec");
-    IR_GUARD(jade::validate(jade::parse_spec_text(spec_json)); return 0;)
+    return jade::c_entry(err, cap, [&] {
+        require(spec_json != nullptr, "null spec");
+        jade::validate(jade::parse_spec_text(spec_json));
+    });
 }
 
 extern "C" int jr_spec_bindings(const char *spec_json, char *out, size_t out_cap, char *err, size_t cap) {
-    clear(err, cap);
-    if (!spec_json) return fail(JR_EINVAL, err, cap, "null spec");
-    IR_GUARD({
-        auto bs = jade::bindings(jade::parse_spec_text(spec_json));
-        jade::Json arr = jade::Json::array();
-        for (auto &b : bs) arr.push(jade::binding_to_json(b));
-        return copy_out(jade::to_string_compact(arr), out, out_cap, err, cap);
-    })
+    return jade::c_entry(err, cap, [&] {
+        require(spec_json != nullptr, "null spec");
+        jade::Json list = jade::Json::array();
+        for (const auto &b : jade::bindings(jade::parse_spec_text(spec_json))) list.push(jade::binding_to_json(b));
+        jade::put_output(jade::to_string_compact(list), out, out_cap);
+    });
 }
 
 extern "C" int jr_spec_validate_bindings(const char *spec_json, const uint64_t *lengths, const uint64_t *ids, size_t count, char *err,
                                          size_t cap) {
-    clear(err, cap);
-    if (!spec_json || (count && (!lengths || !ids))) return fail(JR_EINVAL, err, cap, "null spec or bindings");
-    IR_GUARD({
+    return jade::c_entry(err, cap, [&] {
+        require(spec_json && (!count || (lengths && ids)), "null spec or bindings");
         jade::validate_bindings(jade::parse_spec_text(spec_json), std::vector<uint64_t>(lengths, lengths + count),
                                 std::vector<uint64_t>(ids, ids + count));
-        return 0;
-    })
+    });
 }
 
 extern "C" int jr_spec_launch(const char *spec_json, char *out, size_t out_cap, char *err, size_t cap) {
-    clear(err, cap);
-    if (!spec_json) return fail(JR_EINVAL, err, cap, "null spec");
-    IR_GUARD(return copy_out(jade::to_string_compact(jade::launch_to_json(jade::launch(jade::parse_spec_text(spec_json)))), out, out_cap,
-                             err, cap);)
+    return jade::c_entry(err, cap, [&] {
+        require(spec_json != nullptr, "null spec");
+        jade::put_output(jade::to_string_compact(jade::launch_to_json(jade::launch(jade::parse_spec_text(spec_json)))), out, out_cap);
+    });
 }
 
 extern "C" int jr_spec_emit(const char *spec_json, const char *target, char *out, size_t out_cap, size_t *needed, char *err, size_t cap) {
-    clear(err, cap);
     if (needed) *needed = 0;
-    if (!spec_json || !target) return fail(JR_EINVAL, err, cap, "null spec or target");
-    IR_GUARD({
+    return jade::c_entry(err, cap, [&] {
+        require(spec_json && target, "null spec or target");
         const jade::Spec s = jade::parse_spec_text(spec_json);
-        std::string src;
-        if (!strcmp(target, "corex")) src = jade::corex_source(s);
-        else if (!strcmp(target, "cuda")) src = jade::cuda_elementwise_source(s);
-        else if (!strcmp(target, "metal")) src = jade::metal_source(s);
-        else return fail(JR_EINVAL, err, cap, "unknown emit target `%s` (corex, metal, cuda)", target);
-        if (needed) *needed = src.size() + 1;
-        return copy_out(src, out, out_cap, err, cap);
-    })
+        std::string text;
+        if (!std::strcmp(target, "corex")) text = jade::corex_source(s);
+        else if (!std::strcmp(target, "cuda")) text = jade::cuda_source(s);
+        else if (!std::strcmp(target, "metal")) text = jade::metal_source(s);
+        else raise(JR_EINVAL, "unknown emit target `%s` (corex, metal, cuda)", target);
+        if (needed) *needed = text.size() + 1;
+        jade::put_output(text, out, out_cap);
+    });
 }
 
 extern "C" int jr_spec_canonical(const char *spec_json, char *out, size_t out_cap, char *err, size_t cap) {
-    clear(err, cap);
-    if (!spec_json) return fail(JR_EINVAL, err, cap, "null spec");
-    IR_GUARD(return copy_out(jade::to_string_pretty(jade::spec_to_json(jade::parse_spec_text(spec_json))), out, out_cap, err, cap);)
+    return jade::c_entry(err, cap, [&] {
+        require(spec_json != nullptr, "null spec");
+        jade::put_output(jade::to_string_pretty(jade::spec_to_json(jade::parse_spec_text(spec_json))), out, out_cap);
+    });
 }
 
+namespace {
+// Picks the sm_100a implementation of a validated spec and stores its launch
+// closure, implementation name and path in `k`.
+void select_implementation(Context *ctx, jr_kernel &k) {
+    using jade::Op;
+    const jade::Spec &s = k.spec;
+    std::string why;
+    switch (s.op) {
+        case Op::Elementwise:
+            k.run = jade::make_elementwise_rtc(ctx, s, k.impl);
+            k.path = "nvrtc";
+            return;
+        case Op::Axpy: case Op::Add: case Op::SwiGlu: case Op::RmsNorm: case Op::Softmax: case Op::RmsInv:
+            k.run = jade::make_row_kernel(ctx, s, k.impl);
+            k.path = "simt";
+            return;
+        case Op::Gemm: case Op::GemmSimd:
+            if (s.op == Op::Gemm && s.dtype != jade::DType::F32 && jade::gemm_tc_supports(s, why)) {
+                k.run = jade::make_gemm_tc(ctx, s, k.impl);
+                k.path = "tcgen05";
+            } else {
+                k.run = jade::make_gemm_simt(ctx, s, k.impl);
+                k.path = "simt";
+            }
+            return;
+        case Op::GemmMps:
+            k.run = jade::make_cublas_gemm(ctx, s, k.impl);
+            k.path = "cublas";
+            return;
+        case Op::AttentionOnline: case Op::AttentionScores: case Op::AttentionApply:
+            k.path = s.dtype == jade::DType::F32 ? "simt" : "tcgen05";
+            if (s.dtype == jade::DType::F32) {
+                k.run = jade::make_attention_simt(ctx, s, k.impl);
+            } else if (s.op == Op::AttentionOnline && attention_use_pair(s, ctx->sm_count)) {
+                try {
+                    k.run = jade::make_attention_pair(ctx, s, k.impl);
+                } catch (const jade::IrError &) {  // more work items than the pair kernel's list holds
+                    k.run = jade::make_attention_tc(ctx, s, k.impl);
+                }
+            } else {
+                k.run = jade::make_attention_tc(ctx, s, k.impl);
+            }
+            return;
+        case Op::Fill: case Op::L2Flush:
+            k.run = jade::make_misc_kernel(ctx, s, k.impl);
+            k.path = "simt";
+            return;
+        case Op::AllReduce:
+            k.run = jade::make_all_reduce(ctx, s, k.impl);
+            k.path = "nccl";
+            k.collective = true;
+            return;
+        case Op::Copy: {
+            const cudaMemcpyKind kind = s.direction == "h2d"   ? cudaMemcpyHostToDevice
+                                        : s.direction == "d2h" ? cudaMemcpyDeviceToHost
+                                                               : cudaMemcpyDeviceToDevice;
+            const size_t bytes = s.bytes;
+            k.run = [kind, bytes](cudaStream_t st, void **b) { return cudaMemcpyAsync(b[1], b[0], bytes, kind, st); };
+            k.impl = "copy_" + s.direction;
+            k.path = "copy";
+            return;
+        }
+    }
+}
+}  // namespace
+
 extern "C" int jr_compile(void *handle, const char *spec_json, jr_kernel **out, char *err, size_t cap) {
-    clear(err, cap);
-    if (!out) return fail(JR_EINVAL, err, cap, "null kernel output");
-    *out = nullptr;
-    if (!spec_json) return fail(JR_EINVAL, err, cap, "null spec");
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    auto *k = new (std::nothrow) jr_kernel;
-    if (!k) return fail(JR_ENOMEM, err, cap, "kernel allocation failed");
-    try {
-        k->ctx = ctx;
+    return jade::c_entry(err, cap, [&] {
+        require(out != nullptr, "null kernel output");
+        *out = nullptr;
+        require(spec_json != nullptr, "null spec");
+        Context &ctx = enter(handle);
+        auto k = std::make_unique<jr_kernel>();
+        k->ctx = &ctx;
         k->spec = jade::parse_spec_text(spec_json);
         k->binds = jade::bindings(k->spec);
-        using jade::Op;
-        const jade::Spec &s = k->spec;
-        std::string why;
-        switch (s.op) {
-            case Op::Elementwise: k->run = jade::make_elementwise_rtc(ctx, s, k->impl); k->path = "nvrtc"; break;
-            case Op::Axpy: case Op::Add: case Op::SwiGlu: case Op::RmsNorm: case Op::Softmax: case Op::RmsInv:
-                k->run = jade::make_row_kernel(ctx, s, k->impl);
-                k->path = "simt";
-                break;
-            case Op::Gemm: case Op::GemmSimd:
-                if (s.op == Op::Gemm && s.dtype != jade::DType::F32 && jade::gemm_tc_supports(s, why)) {
-                    k->run = jade::make_gemm_tc(ctx, s, k->impl);
-                    k->path = "tcgen05";
-                } else {
-                    k->run = jade::make_gemm_simt(ctx, s, k->impl);
-                    k->path = "simt";
-                }
-                break;
-            case Op::GemmMps: k->run = jade::make_cublas_gemm(ctx, s, k->impl); k->path = "cublas"; break;
-            case Op::AttentionOnline: case Op::AttentionScores: case Op::AttentionApply:
-                if (s.dtype == jade::DType::F32) {
-                    k->run = jade::make_attention_simt(ctx, s, k->impl);
-                    k->path = "simt";
-                } else if (s.op == Op::AttentionOnline && attention_use_pair(s, ctx->sm_count)) {
-                    try {
-                        k->run = jade::make_attention_pair(ctx, s, k->impl);
-                    } catch (const jade::IrError &) {  // more work items than the pair kernel's list holds
-                        k->run = jade::make_attention_tc(ctx, s, k->impl);
-                    }
-                    k->path = "tcgen05";
-                } else {
-                    k->run = jade::make_attention_tc(ctx, s, k->impl);
-                    k->path = "tcgen05";
-                }
-                break;
-            case Op::Fill: case Op::L2Flush: k->run = jade::make_misc_kernel(ctx, s, k->impl); k->path = "simt"; break;
-            case Op::AllReduce:
-                k->run = jade::make_all_reduce(ctx, s, k->impl);
-                k->path = "nccl";
-                k->collective = true;
-                break;
-            case Op::Copy: {
-                const cudaMemcpyKind kind = s.direction == "h2d" ? cudaMemcpyHostToDevice
-                                            : s.direction == "d2h" ? cudaMemcpyDeviceToHost
-                                                                   : cudaMemcpyDeviceToDevice;
-                const size_t bytes = s.bytes;
-                k->run = [kind, bytes](cudaStream_t st, void **b) { return cudaMemcpyAsync(b[1], b[0], bytes, kind, st); };
-                k->impl = "copy_" + s.direction;
-                k->path = "copy";
-                break;
-            }
-        }
-    } catch (const std::exception &e) {
-        delete k;
-        return fail(JR_EINVAL, err, cap, "%s", e.what());
-    }
-    const auto st = cudaGetLastError();
-    if (st != cudaSuccess) {
-        delete k;
-        return cuda_fail(st, err, cap, "kernel setup");
-    }
-    *out = k;
-    return 0;
+        select_implementation(&ctx, *k);
+        check_cuda(cudaGetLastError(), "kernel setup");
+        *out = k.release();
+    });
 }
 
 extern "C" void jr_kernel_release(jr_kernel *kernel) { delete kernel; }
 
 extern "C" int jr_kernel_info(jr_kernel *k, char *out, size_t out_cap, char *err, size_t cap) {
-    clear(err, cap);
-    if (!k) return fail(JR_EINVAL, err, cap, "null kernel");
-    jade::Json j = jade::Json::object();
-    j.set("name", jade::Json::str(jade::spec_name(k->spec))).set("impl", jade::Json::str(k->impl)).set("path", jade::Json::str(k->path));
-    j.set("spec", jade::spec_to_json(k->spec));
-    jade::Json arr = jade::Json::array();
-    for (auto &b : k->binds) arr.push(jade::binding_to_json(b));
-    j.set("bindings", arr);
-    return copy_out(jade::to_string_compact(j), out, out_cap, err, cap);
+    return jade::c_entry(err, cap, [&] {
+        require(k != nullptr, "null kernel");
+        jade::Json binds = jade::Json::array();
+        for (const auto &b : k->binds) binds.push(jade::binding_to_json(b));
+        jade::Json info = jade::Json::object();
+        info.set("name", jade::Json::str(jade::spec_name(k->spec)))
+            .set("impl", jade::Json::str(k->impl))
+            .set("path", jade::Json::str(k->path))
+            .set("spec", jade::spec_to_json(k->spec))
+            .set("bindings", binds);
+        jade::put_output(jade::to_string_compact(info), out, out_cap);
+    });
 }
 
 namespace {
-int validate_dispatch(Context *ctx, const jr_dispatch *jobs, size_t n, char *err, size_t cap) {
+
+// Registry checks of one batch, all before any launch: each kernel belongs to
+// this context, each binding is a buffer this context allocated, of the memory
+// kind and exact byte size the spec declares, and no output aliases another
+// binding of its job.
+void check_batch(Context &ctx, const jr_dispatch *jobs, size_t n) {
     for (size_t j = 0; j < n; ++j) {
         const jr_dispatch &d = jobs[j];
-        if (!d.kernel) return fail(JR_EINVAL, err, cap, "job %zu: null kernel", j);
-        if (d.kernel->ctx != ctx) return fail(JR_EINVAL, err, cap, "job %zu: kernel belongs to another runtime/device context", j);
+        if (!d.kernel) raise(JR_EINVAL, "job %zu: null kernel", j);
+        if (d.kernel->ctx != &ctx) raise(JR_EINVAL, "job %zu: kernel belongs to another runtime/device context", j);
         const auto &binds = d.kernel->binds;
-        if (!d.buffers || d.buffer_count != binds.size())
-            return fail(JR_EINVAL, err, cap, "job %zu: %s expects %zu bindings", j, jade::spec_name(d.kernel->spec), binds.size());
+        const char *kname = jade::spec_name(d.kernel->spec);
+        if (!d.buffers || d.buffer_count != binds.size()) raise(JR_EINVAL, "job %zu: %s expects %zu bindings", j, kname, binds.size());
         for (size_t b = 0; b < binds.size(); ++b) {
+            const jade::Binding &bind = binds[b];
             const void *p = d.buffers[b];
-            if (!p) return fail(JR_EINVAL, err, cap, "job %zu: null buffer %zu", j, b);
-            auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(p));
-            if (it == ctx->allocations.end())
-                return fail(JR_EINVAL, err, cap, "job %zu: buffer %s belongs to another runtime/device context", j, binds[b].name.c_str());
-            if (it->second.host != binds[b].host)
-                return fail(JR_EINVAL, err, cap, "job %zu: buffer %s must be %s memory", j, binds[b].name.c_str(),
-                            binds[b].host ? "pinned host" : "device");
-            const uint64_t want = binds[b].elements * jade::dtype_size(binds[b].dtype);
-            if (it->second.bytes != want)
-                return fail(JR_EINVAL, err, cap, "job %zu: %s binding %s expected %llu bytes (%llu %s), got %zu", j,
-                            jade::spec_name(d.kernel->spec), binds[b].name.c_str(), (unsigned long long)want,
-                            (unsigned long long)binds[b].elements, jade::dtype_name(binds[b].dtype), it->second.bytes);
+            if (!p) raise(JR_EINVAL, "job %zu: null buffer %zu", j, b);
+            const auto reg = ctx.allocations.find(reinterpret_cast<uintptr_t>(p));
+            if (reg == ctx.allocations.end())
+                raise(JR_EINVAL, "job %zu: buffer %s belongs to another runtime/device context", j, bind.name.c_str());
+            if (reg->second.host != bind.host)
+                raise(JR_EINVAL, "job %zu: buffer %s must be %s memory", j, bind.name.c_str(), bind.host ? "pinned host" : "device");
+            const uint64_t want = bind.elements * jade::dtype_size(bind.dtype);
+            if (reg->second.bytes != want)
+                raise(JR_EINVAL, "job %zu: %s binding %s expected %llu bytes (%llu %s), got %zu", j, kname, bind.name.c_str(),
+                      (unsigned long long)want, (unsigned long long)bind.elements, jade::dtype_name(bind.dtype), reg->second.bytes);
+            if (bind.write && std::count(d.buffers, d.buffers + binds.size(), p) > 1)
+                raise(JR_EINVAL, "job %zu: output binding must not alias another binding", j);
+        }
+    }
+}
+
+// Per-launch timing events, grown on demand and kept by the context.
+void reserve_events(std::vector<cudaEvent_t> &pool, size_t need, unsigned flags, const char *what) {
+    while (pool.size() < need) {
+        cudaEvent_t e;
+        check_cuda(cudaEventCreateWithFlags(&e, flags), what);
+        pool.push_back(e);
+    }
+}
+
+// A captured pass of the batch, instantiated once and released on every path.
+struct CapturedPass {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    ~CapturedPass() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+    }
+    void capture(cudaStream_t s, const jr_dispatch *jobs, size_t n) {
+        check_cuda(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin graph capture");
+        cudaError_t st = cudaSuccess;
+        for (size_t j = 0; j < n && st == cudaSuccess; ++j) st = jobs[j].kernel->run(s, jobs[j].buffers);
+        const cudaError_t end = cudaStreamEndCapture(s, &graph);
+        if (st != cudaSuccess || end != cudaSuccess) {
+            cudaGetLastError();
+            check_cuda(st != cudaSuccess ? st : end, "graph capture");
+        }
+        check_cuda(cudaGraphInstantiate(&exec, graph, 0), "graph instantiate");
+    }
+};
+
+// JR_EXEC_STREAMS placement: lane 0 is the context stream, lane 1 takes
+// host-to-device copies and lane 2 device-to-host copies. Every launch records
+// an event; before a launch, its lane waits for the latest conflicting launch on
+// each other lane (a write to a buffer it touches; for an output, also reads of
+// it since that write). Launches within a lane are already ordered, so the
+// latest conflicting launch per lane is all that needs waiting for.
+class LaneScheduler {
+  public:
+    LaneScheduler(Context &ctx, size_t launches) : ctx_(ctx) {
+        lane_stream_[0] = ctx.stream;
+        lane_stream_[1] = ctx.copy_in;
+        lane_stream_[2] = ctx.copy_out;
+        for (auto &row : waited_) std::fill(std::begin(row), std::end(row), -1L);
+        lane_of_.reserve(launches);
+        for (int l = 1; l < kLanes; ++l) check_cuda(cudaStreamWaitEvent(lane_stream_[l], ctx.start, 0), "kernel launch");
+    }
+
+    // Makes `job`'s lane wait for its hazards, launches it (between the timing
+    // events `before` and `after` when given), records its dependency event.
+    void launch(const jr_dispatch &job, cudaEvent_t before, cudaEvent_t after) {
+        const jade::Spec &sp = job.kernel->spec;
+        int lane = 0;
+        if (sp.op == jade::Op::Copy) lane = sp.direction == "h2d" ? 1 : sp.direction == "d2h" ? 2 : 0;
+        long hazard[kLanes] = {-1, -1, -1};
+        const auto &binds = job.kernel->binds;
+        for (size_t b = 0; b < binds.size(); ++b) {
+            const Uses &u = uses_[job.buffers[b]];
+            if (u.writer >= 0) hazard[lane_of_[u.writer]] = std::max(hazard[lane_of_[u.writer]], u.writer);
             if (binds[b].write)
-                for (size_t o = 0; o < binds.size(); ++o)
-                    if (o != b && d.buffers[o] == p) return fail(JR_EINVAL, err, cap, "job %zu: output binding must not alias another binding", j);
+                for (int l = 0; l < kLanes; ++l) hazard[l] = std::max(hazard[l], u.reader[l]);
+        }
+        for (int l = 0; l < kLanes; ++l)
+            if (l != lane && hazard[l] > waited_[lane][l]) {
+                check_cuda(cudaStreamWaitEvent(lane_stream_[lane], ctx_.dep_events[hazard[l]], 0), "kernel launch");
+                waited_[lane][l] = hazard[l];
+            }
+        const long id = (long)lane_of_.size();
+        if (before) cudaEventRecord(before, lane_stream_[lane]);
+        check_cuda(job.kernel->run(lane_stream_[lane], job.buffers), "kernel launch");
+        if (after) cudaEventRecord(after, lane_stream_[lane]);
+        check_cuda(cudaEventRecord(ctx_.dep_events[id], lane_stream_[lane]), "kernel launch");
+        lane_of_.push_back(lane);
+        last_[lane] = id;
+        for (size_t b = 0; b < binds.size(); ++b) {
+            Uses &u = uses_[job.buffers[b]];
+            if (binds[b].write) u = Uses{id, {-1, -1, -1}};
+            else u.reader[lane] = id;
         }
     }
-    return 0;
-}
 
-// Waits for `ev` without blocking forever when collectives are in flight.
-int wait_event(Context *ctx, cudaEvent_t ev, bool collective, char *err, size_t cap);
-}  // namespace
-
-namespace jade {
-int comm_poll_abort(Context *ctx, char *err, size_t cap);  // comm.cpp
-}
-
-namespace {
-int wait_event(Context *ctx, cudaEvent_t ev, bool collective, char *err, size_t cap) {
-    if (!collective) {
-        const auto st = cudaEventSynchronize(ev);
-        return st == cudaSuccess ? 0 : cuda_fail(st, err, cap, "kernel synchronization");
+    // The context stream joins the transfer lanes (before the stop event).
+    void join() {
+        for (int l = 1; l < kLanes; ++l)
+            if (last_[l] >= 0) check_cuda(cudaStreamWaitEvent(ctx_.stream, ctx_.dep_events[last_[l]], 0), "kernel launch");
     }
-    const auto t0 = std::chrono::steady_clock::now();
-    while (true) {
-        const auto st = cudaEventQuery(ev);
-        if (st == cudaSuccess) return 0;
-        if (st != cudaErrorNotReady) return cuda_fail(st, err, cap, "kernel synchronization");
-        const int rc = jade::comm_poll_abort(ctx, err, cap);
-        if (rc) return rc;
-        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
-        if ((uint64_t)ms > ctx->comm_timeout_ms) {
-            jade::comm_destroy(ctx);  // aborts the communicator so queued collectives return
-            cudaStreamSynchronize(ctx->stream);
-            return fail(JR_ETIMEOUT, err, cap, "collective did not complete within %u ms; communicator aborted", ctx->comm_timeout_ms);
-        }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+
+    void drain() {
+        for (cudaStream_t s : lane_stream_) cudaStreamSynchronize(s);
     }
-}
+
+  private:
+    static constexpr int kLanes = 3;
+    struct Uses {
+        long writer = -1;
+        long reader[kLanes] = {-1, -1, -1};
+    };
+    Context &ctx_;
+    cudaStream_t lane_stream_[kLanes];
+    std::map<const void *, Uses> uses_;
+    std::vector<int> lane_of_;
+    long waited_[kLanes][kLanes];
+    long last_[kLanes] = {-1, -1, -1};
+};
+
 }  // namespace
 
 extern "C" int jr_execute2(void *handle, const jr_dispatch *jobs, size_t job_count, uint32_t repeats, uint32_t flags, double *gpu_ms,
                            double *job_ms, char *err, size_t cap) {
-    clear(err, cap);
     if (gpu_ms) *gpu_ms = 0;
-    if (!jobs || !job_count || !repeats || !gpu_ms) return fail(JR_EINVAL, err, cap, "empty dispatch sequence or missing timing output");
-    const bool graph = flags & JR_EXEC_GRAPH, streams = flags & JR_EXEC_STREAMS;
-    if (flags & ~(JR_EXEC_GRAPH | JR_EXEC_STREAMS)) return fail(JR_EINVAL, err, cap, "unknown execution flags 0x%x", flags);
-    if (graph && job_ms) return fail(JR_EINVAL, err, cap, "per-job timing is not available with graph replay");
-    if (graph && streams) return fail(JR_EINVAL, err, cap, "graph replay and dependency-scheduled streams cannot be combined");
-    auto *ctx = static_cast<Context *>(handle);
-    if (!ctx) return fail(JR_EINVAL, err, cap, "null runtime context");
-    int rc = validate_dispatch(ctx, jobs, job_count, err, cap);
-    if (rc) return rc;
-    rc = select(ctx, err, cap);
-    if (rc) return rc;
-    bool collective = false;
-    for (size_t j = 0; j < job_count; ++j) collective |= jobs[j].kernel->collective;
-    if (job_ms) {
-        for (size_t j = 0; j < job_count; ++j) job_ms[j] = 0;
-        const size_t need = 2 * job_count * repeats;
-        if (need > 65536) return fail(JR_EINVAL, err, cap, "per-job timing supports at most 32768 job launches per call");
-        while (ctx->job_events.size() < need) {
-            cudaEvent_t e;
-            const auto st = cudaEventCreate(&e);
-            if (st != cudaSuccess) return cuda_fail(st, err, cap, "create job events");
-            ctx->job_events.push_back(e);
+    return jade::c_entry(err, cap, [&] {
+        require(jobs && job_count && repeats && gpu_ms, "empty dispatch sequence or missing timing output");
+        const bool graph = flags & JR_EXEC_GRAPH, lanes = flags & JR_EXEC_STREAMS;
+        if (flags & ~(JR_EXEC_GRAPH | JR_EXEC_STREAMS)) raise(JR_EINVAL, "unknown execution flags 0x%x", flags);
+        require(!(graph && job_ms), "per-job timing is not available with graph replay");
+        require(!(graph && lanes), "graph replay and dependency-scheduled streams cannot be combined");
+        auto *raw = static_cast<Context *>(handle);
+        require(raw != nullptr, "null runtime context");
+        check_batch(*raw, jobs, job_count);
+        Context &ctx = enter(handle);
+        const bool collective = std::any_of(jobs, jobs + job_count, [](const jr_dispatch &d) { return d.kernel->collective; });
+        const size_t launches = job_count * (size_t)repeats;
+        if (job_ms) {
+            std::fill(job_ms, job_ms + job_count, 0.0);
+            if (2 * launches > 65536) raise(JR_EINVAL, "per-job timing supports at most 32768 job launches per call");
+            reserve_events(ctx.job_events, 2 * launches, cudaEventDefault, "create job events");
         }
-    }
-    if (streams) {
-        const size_t need = job_count * repeats;
-        if (need > 65536) return fail(JR_EINVAL, err, cap, "dependency-scheduled streams support at most 65536 job launches per call");
-        cudaError_t st = cudaSuccess;
-        if (!ctx->copy_in) st = cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking);
-        if (st == cudaSuccess && !ctx->copy_out) st = cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking);
-        while (st == cudaSuccess && ctx->dep_events.size() < need) {
-            cudaEvent_t e;
-            st = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
-            if (st == cudaSuccess) ctx->dep_events.push_back(e);
+        if (lanes) {
+            if (launches > 65536) raise(JR_EINVAL, "dependency-scheduled streams support at most 65536 job launches per call");
+            const char *what = "create transfer streams/dependency events";
+            for (cudaStream_t *s : {&ctx.copy_in, &ctx.copy_out})
+                if (!*s) check_cuda(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), what);
+            reserve_events(ctx.dep_events, launches, cudaEventDisableTiming, what);
         }
-        if (st != cudaSuccess) return cuda_fail(st, err, cap, "create transfer streams/dependency events");
-    }
-    cudaError_t status;
-    cudaGraphExec_t exec = nullptr;
-    cudaGraph_t g = nullptr;
-    if (graph) {
-        status = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
-        if (status != cudaSuccess) return cuda_fail(status, err, cap, "begin graph capture");
-        for (size_t j = 0; j < job_count && status == cudaSuccess; ++j) status = jobs[j].kernel->run(ctx->stream, jobs[j].buffers);
-        const auto end = cudaStreamEndCapture(ctx->stream, &g);
-        if (status != cudaSuccess || end != cudaSuccess) {
-            if (g) cudaGraphDestroy(g);
-            cudaGetLastError();
-            return cuda_fail(status != cudaSuccess ? status : end, err, cap, "graph capture");
-        }
-        status = cudaGraphInstantiate(&exec, g, 0);
-        if (status != cudaSuccess) {
-            cudaGraphDestroy(g);
-            return cuda_fail(status, err, cap, "graph instantiate");
-        }
-    }
-    status = cudaEventRecord(ctx->start, ctx->stream);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "record start event");
-    // JR_EXEC_STREAMS: stream 0 = context stream, 1 = transfers in, 2 = transfers out.
-    // Per buffer, the last writing launch and the last reading launch on each stream
-    // since that write (launches on one stream are ordered, so the last one suffices).
-    struct Access {
-        long write = -1;
-        long read[3] = {-1, -1, -1};
-    };
-    std::map<const void *, Access> access;
-    std::vector<int> launch_stream;
-    long waited[3][3];  // [stream][source stream]: latest launch already waited for
-    long last_on[3] = {-1, -1, -1};
-    cudaStream_t stream_of[3] = {ctx->stream, ctx->copy_in, ctx->copy_out};
-    if (streams) {
-        for (auto &w : waited)
-            for (long &x : w) x = -1;
-        launch_stream.reserve(job_count * repeats);
-        status = cudaStreamWaitEvent(ctx->copy_in, ctx->start, 0);
-        if (status == cudaSuccess) status = cudaStreamWaitEvent(ctx->copy_out, ctx->start, 0);
-    }
-    size_t ev = 0;
-    long launch = 0;
-    for (uint32_t r = 0; r < repeats && status == cudaSuccess; ++r) {
-        if (graph) {
-            status = cudaGraphLaunch(exec, ctx->stream);
-            continue;
-        }
-        for (size_t j = 0; j < job_count; ++j) {
-            int sid = 0;
-            if (streams) {
-                const jade::Spec &sp = jobs[j].kernel->spec;
-                if (sp.op == jade::Op::Copy) sid = sp.direction == "h2d" ? 1 : sp.direction == "d2h" ? 2 : 0;
-                long need[3] = {-1, -1, -1};
-                const auto &binds = jobs[j].kernel->binds;
-                for (size_t b = 0; b < binds.size(); ++b) {
-                    const Access &a = access[jobs[j].buffers[b]];
-                    if (a.write >= 0) need[launch_stream[a.write]] = std::max(need[launch_stream[a.write]], a.write);
-                    if (binds[b].write)
-                        for (int t = 0; t < 3; ++t) need[t] = std::max(need[t], a.read[t]);
+        CapturedPass pass;
+        if (graph) pass.capture(ctx.stream, jobs, job_count);
+        check_cuda(cudaEventRecord(ctx.start, ctx.stream), "record start event");
+        std::unique_ptr<LaneScheduler> sched;
+        try {
+            if (lanes) sched = std::make_unique<LaneScheduler>(ctx, launches);
+            size_t ev = 0;
+            for (uint32_t r = 0; r < repeats; ++r) {
+                if (graph) {
+                    check_cuda(cudaGraphLaunch(pass.exec, ctx.stream), "kernel launch");
+                    continue;
                 }
-                for (int t = 0; t < 3 && status == cudaSuccess; ++t)
-                    if (t != sid && need[t] > waited[sid][t]) {
-                        status = cudaStreamWaitEvent(stream_of[sid], ctx->dep_events[need[t]], 0);
-                        waited[sid][t] = need[t];
+                for (size_t j = 0; j < job_count; ++j, ev += 2) {
+                    cudaEvent_t before = job_ms ? ctx.job_events[ev] : nullptr;
+                    cudaEvent_t after = job_ms ? ctx.job_events[ev + 1] : nullptr;
+                    if (sched) {
+                        sched->launch(jobs[j], before, after);
+                        continue;
                     }
-                if (status != cudaSuccess) break;
-            }
-            cudaStream_t st = stream_of[sid];
-            if (job_ms) cudaEventRecord(ctx->job_events[ev++], st);
-            status = jobs[j].kernel->run(st, jobs[j].buffers);
-            if (job_ms) cudaEventRecord(ctx->job_events[ev++], st);
-            if (status != cudaSuccess) break;
-            if (streams) {
-                status = cudaEventRecord(ctx->dep_events[launch], st);
-                launch_stream.push_back(sid);
-                last_on[sid] = launch;
-                const auto &binds = jobs[j].kernel->binds;
-                for (size_t b = 0; b < binds.size(); ++b) {
-                    Access &a = access[jobs[j].buffers[b]];
-                    if (binds[b].write) {
-                        a.write = launch;
-                        a.read[0] = a.read[1] = a.read[2] = -1;
-                    } else {
-                        a.read[sid] = launch;
-                    }
+                    if (before) cudaEventRecord(before, ctx.stream);
+                    check_cuda(jobs[j].kernel->run(ctx.stream, jobs[j].buffers), "kernel launch");
+                    if (after) cudaEventRecord(after, ctx.stream);
                 }
-                ++launch;
-                if (status != cudaSuccess) break;
             }
+            if (sched) sched->join();
+        } catch (const Fault &) {
+            if (sched) sched->drain();
+            cudaStreamSynchronize(ctx.stream);
+            throw;
         }
-    }
-    if (streams)  // the context stream joins the transfer streams before the stop event
-        for (int t = 1; t < 3 && status == cudaSuccess; ++t)
-            if (last_on[t] >= 0) status = cudaStreamWaitEvent(ctx->stream, ctx->dep_events[last_on[t]], 0);
-    if (status != cudaSuccess) {
-        if (streams) {
-            cudaStreamSynchronize(ctx->copy_in);
-            cudaStreamSynchronize(ctx->copy_out);
+        const cudaError_t stop = cudaEventRecord(ctx.stop, ctx.stream);
+        if (stop != cudaSuccess) {
+            cudaStreamSynchronize(ctx.stream);
+            check_cuda(stop, "record stop event");
         }
-        cudaStreamSynchronize(ctx->stream);
-        if (exec) cudaGraphExecDestroy(exec);
-        if (g) cudaGraphDestroy(g);
-        return cuda_fail(status, err, cap, "kernel launch");
-    }
-    status = cudaEventRecord(ctx->stop, ctx->stream);
-    if (status != cudaSuccess) {
-        cudaStreamSynchronize(ctx->stream);
-        return cuda_fail(status, err, cap, "record stop event");
-    }
-    rc = wait_event(ctx, ctx->stop, collective, err, cap);
-    if (exec) cudaGraphExecDestroy(exec);
-    if (g) cudaGraphDestroy(g);
-    if (rc) return rc;
-    rc = check_device_error(ctx, err, cap);
-    if (rc) return rc;
-    float elapsed = 0;
-    status = cudaEventElapsedTime(&elapsed, ctx->start, ctx->stop);
-    if (status != cudaSuccess) return cuda_fail(status, err, cap, "event elapsed time");
-    if (!std::isfinite(elapsed) || elapsed < 0) return fail(JR_ECUDA, err, cap, "invalid GPU-event duration");
-    *gpu_ms = elapsed;
-    if (job_ms) {
-        ev = 0;
-        for (uint32_t r = 0; r < repeats; ++r)
-            for (size_t j = 0; j < job_count; ++j) {
+        await_event(ctx, ctx.stop, collective);
+        raise_device_wait_error(ctx);
+        *gpu_ms = bracket_ms(ctx);
+        if (job_ms)
+            for (size_t launch = 0; launch < launches; ++launch) {
                 float t = 0;
-                cudaEventElapsedTime(&t, ctx->job_events[ev], ctx->job_events[ev + 1]);
-                ev += 2;
-                job_ms[j] += t;
+                cudaEventElapsedTime(&t, ctx.job_events[2 * launch], ctx.job_events[2 * launch + 1]);
+                job_ms[launch % job_count] += t;
             }
-    }
-    return 0;
+    });
 }
 
 extern "C" int jr_buffer_bytes(void *handle, const void *ptr, size_t *bytes) {
     auto *ctx = static_cast<Context *>(handle);
     if (!ctx || !ptr || !bytes) return JR_EINVAL;
-    auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(ptr));
+    const auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(ptr));
     if (it == ctx->allocations.end()) return JR_EINVAL;
     *bytes = it->second.bytes;
-    return 0;
+    return JR_OK;
 }
 
 extern "C" int jr_host_alloc(void *handle, size_t bytes, void **out, char *err, size_t cap) {
-    clear(err, cap);
-    if (!out) return fail(JR_EINVAL, err, cap, "null allocation output");
-    *out = nullptr;
-    if (!bytes) return fail(JR_EINVAL, err, cap, "allocation must be nonempty");
-    auto *ctx = static_cast<Context *>(handle);
-    const int rc = select(ctx, err, cap);
-    if (rc) return rc;
-    const auto status = cudaMallocHost(out, bytes);
-    if (status != cudaSuccess) {
-        cudaGetLastError();
+    return jade::c_entry(err, cap, [&] {
+        require(out != nullptr, "null allocation output");
         *out = nullptr;
-        return fail(JR_ENOMEM, err, cap, "cudaMallocHost: %s", cudaGetErrorString(status));
-    }
-    memset(*out, 0, bytes);
-    ctx->allocations[reinterpret_cast<uintptr_t>(*out)] = jade::Allocation{bytes, true};
-    return 0;
+        require(bytes != 0, "allocation must be nonempty");
+        Context &ctx = enter(handle);
+        void *p = nullptr;
+        const cudaError_t st = cudaMallocHost(&p, bytes);
+        if (st != cudaSuccess) {
+            cudaGetLastError();
+            raise(JR_ENOMEM, "cudaMallocHost: %s", cudaGetErrorString(st));
+        }
+        std::memset(p, 0, bytes);
+        ctx.allocations[reinterpret_cast<uintptr_t>(p)] = jade::Allocation{bytes, true};
+        *out = p;
+    });
 }
 
 extern "C" void jr_host_free(void *handle, void *ptr) {
     auto *ctx = static_cast<Context *>(handle);
     if (!ctx || !ptr) return;
-    auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(ptr));
+    const auto it = ctx->allocations.find(reinterpret_cast<uintptr_t>(ptr));
     if (it == ctx->allocations.end() || !it->second.host) return;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);

@@ -312,15 +312,20 @@ class Runtime:
         e = _err()
         _check(lib().jr_upload(self.ctx, buf.ptr, arr.ctypes.data, buf.nbytes, e, len(e)), e)
 
-    def download(self, buf: Buffer) -> np.ndarray:
+    def download(self, buf: Buffer, start: int = 0, count: int | None = None) -> np.ndarray:
+        """Elements [start, start+count) of a buffer (all of it by default)."""
         self._own(buf)
-        out = np.empty(buf.elements, dtype=NP_DTYPE[buf.dtype])
+        count = buf.elements - start if count is None else count
+        if start < 0 or count < 1 or start + count > buf.elements:
+            raise ValueError(f"range [{start}, {start + count}) outside a buffer of {buf.elements} elements")
+        out = np.empty(count, dtype=NP_DTYPE[buf.dtype])
+        size = out.itemsize
         e = _err()
-        _check(lib().jr_download(self.ctx, buf.ptr, out.ctypes.data, buf.nbytes, e, len(e)), e)
+        _check(lib().jr_download(self.ctx, buf.ptr + start * size, out.ctypes.data, count * size, e, len(e)), e)
         return out
 
-    def download_f32(self, buf: Buffer) -> np.ndarray:
-        out = self.download(buf)
+    def download_f32(self, buf: Buffer, start: int = 0, count: int | None = None) -> np.ndarray:
+        out = self.download(buf, start, count)
         if buf.dtype == "bf16":
             return bf16_to_f32(out)
         return out.astype(np.float32)

@@ -124,6 +124,7 @@ int or_validation_check(size_t m, size_t n, size_t k, const float *a, const floa
         const double tolerance = 2e-5 + coefficient * sum_abs;
         if (error > r->max_abs_error) r->max_abs_error = error;
         if (error / tolerance > r->max_scaled_error) r->max_scaled_error = error / tolerance;
+        if (sum_abs > 0 && error / sum_abs > r->max_magnitude_error) r->max_magnitude_error = error / sum_abs;
         if (!(error <= tolerance)) {
             r->first_bad_index = (int64_t)idx;
             return 1;
@@ -215,9 +216,12 @@ void or_add_fp32(size_t n, const float *a, const float *b, float *out) {
     }
 }
 
-/* metal_lab.rs:33-73, one (head, row) */
+/* metal_lab.rs:33-73, one (head, row). When mag is given it also receives, per
+ * output element d, sum_col p[col]*|v[col][d]| (p the softmax weights): the
+ * magnitude that scales the rounding error of a weighted sum (validation.rs:35-91
+ * uses sum|a*b| the same way for GEMM). */
 static void attention_one(size_t seq, size_t dim, int causal, const float *qh, const float *kh,
-                          const float *vh, size_t row, double *scores, double *o) {
+                          const float *vh, size_t row, double *scores, double *o, double *mag) {
     const size_t count = causal ? row + 1 : seq;
     const double sd = sqrt((double)dim);
     for (size_t col = 0; col < count; ++col) {
@@ -231,9 +235,14 @@ static void attention_one(size_t seq, size_t dim, int causal, const float *qh, c
     double denom = 0.0;
     for (size_t col = 0; col < count; ++col) denom += scores[col];
     for (size_t d = 0; d < dim; ++d) {
-        double acc = 0.0;
-        for (size_t col = 0; col < count; ++col) acc += scores[col] / denom * (double)vh[col * dim + d];
+        double acc = 0.0, size = 0.0;
+        for (size_t col = 0; col < count; ++col) {
+            const double p = scores[col] / denom, v = (double)vh[col * dim + d];
+            acc += p * v;
+            size += p * fabs(v);
+        }
         o[d] = acc;
+        if (mag) mag[d] = size;
     }
 }
 
@@ -249,15 +258,15 @@ void or_attention(size_t bh, size_t seq, size_t dim, int causal, const float *q,
             const size_t h = (size_t)t / seq, row = (size_t)t % seq;
             const size_t base = h * seq * dim;
             attention_one(seq, dim, causal, q + base, k + base, v + base, row, scores,
-                          out + base + row * dim);
+                          out + base + row * dim, NULL);
         }
         free(scores);
     }
 }
 
-void or_attention_rows(size_t seq, size_t dim, int causal, const float *q, const float *k,
-                       const float *v, const int64_t *bh_idx, const int64_t *row_idx,
-                       size_t npairs, double *out, int threads) {
+void or_attention_rows_bound(size_t seq, size_t dim, int causal, const float *q, const float *k,
+                             const float *v, const int64_t *bh_idx, const int64_t *row_idx,
+                             size_t npairs, double *out, double *mag, int threads) {
     long long total = (long long)npairs;
 #pragma omp parallel num_threads(clamp_threads(threads))
     {
@@ -266,16 +275,30 @@ void or_attention_rows(size_t seq, size_t dim, int causal, const float *q, const
         for (long long t = 0; t < total; ++t) {
             const size_t base = (size_t)bh_idx[t] * seq * dim;
             attention_one(seq, dim, causal, q + base, k + base, v + base, (size_t)row_idx[t],
-                          scores, out + (size_t)t * dim);
+                          scores, out + (size_t)t * dim, mag ? mag + (size_t)t * dim : NULL);
         }
         free(scores);
     }
 }
 
-/* workloads.rs:466-479 for a subset of token rows */
-void or_mlp_rows(size_t width, size_t hidden, const float *x, const float *norm_weight,
-                 const float *wg, const float *wu, const float *wd, double eps,
-                 const int64_t *rows, size_t nrows, double *out, int threads) {
+void or_attention_rows(size_t seq, size_t dim, int causal, const float *q, const float *k,
+                       const float *v, const int64_t *bh_idx, const int64_t *row_idx,
+                       size_t npairs, double *out, int threads) {
+    or_attention_rows_bound(seq, dim, causal, q, k, v, bh_idx, row_idx, npairs, out, NULL, threads);
+}
+
+float or_bf16_to_f32(uint16_t h);
+uint16_t or_f32_to_bf16(float x);
+
+/* workloads.rs:466-479 for a subset of token rows. round_h != 0 rounds the
+ * activation h = silu(g)*u to BF16 before the down projection, the point where a
+ * BF16 pipeline stores it; mag (optional) receives per output element
+ * sum_p |h_p*wd[p][c]| + |x_c|, the magnitude of the down projection and
+ * residual sums. */
+void or_mlp_rows_ex(size_t width, size_t hidden, const float *x, const float *norm_weight,
+                    const float *wg, const float *wu, const float *wd, double eps,
+                    const int64_t *rows, size_t nrows, int round_h, double *out, double *mag,
+                    int threads) {
     long long cnt = (long long)nrows;
 #pragma omp parallel num_threads(clamp_threads(threads))
     {
@@ -299,13 +322,21 @@ void or_mlp_rows(size_t width, size_t hidden, const float *x, const float *norm_
                     u[j] += a * (double)wur[j];
                 }
             }
-            for (size_t j = 0; j < hidden; ++j) g[j] = g[j] * or_sigmoid(g[j]) * u[j];
+            for (size_t j = 0; j < hidden; ++j) {
+                g[j] = g[j] * or_sigmoid(g[j]) * u[j];
+                if (round_h) g[j] = (double)or_bf16_to_f32(or_f32_to_bf16((float)g[j]));
+            }
             double *o = out + (size_t)r * width;
+            double *mg = mag ? mag + (size_t)r * width : NULL;
             for (size_t c = 0; c < width; ++c) o[c] = 0.0;
+            if (mg)
+                for (size_t c = 0; c < width; ++c) mg[c] = fabs((double)xr[c]);
             for (size_t p = 0; p < hidden; ++p) {
                 const double a = g[p];
                 const float *wdr = wd + p * width;
                 for (size_t c = 0; c < width; ++c) o[c] += a * (double)wdr[c];
+                if (mg)
+                    for (size_t c = 0; c < width; ++c) mg[c] += fabs(a * (double)wdr[c]);
             }
             for (size_t c = 0; c < width; ++c) o[c] += (double)xr[c];
         }
@@ -313,6 +344,12 @@ void or_mlp_rows(size_t width, size_t hidden, const float *x, const float *norm_
         free(g);
         free(u);
     }
+}
+
+void or_mlp_rows(size_t width, size_t hidden, const float *x, const float *norm_weight,
+                 const float *wg, const float *wu, const float *wd, double eps,
+                 const int64_t *rows, size_t nrows, double *out, int threads) {
+    or_mlp_rows_ex(width, hidden, x, norm_weight, wg, wu, wd, eps, rows, nrows, 0, out, NULL, threads);
 }
 
 /* IEEE round-to-nearest-even narrowing, restated from the binary formats. */

@@ -34,6 +34,13 @@ void or_gemm_reference(size_t m, size_t n, size_t k, const float *a, const float
 /* FP64 GEMM restricted to listed rows (for sampled checks at large sizes). */
 void or_gemm_rows(size_t n, size_t k, const float *a, const float *b,
                   const int64_t *rows, size_t nrows, double *out, int threads);
+/* The same chain with h = silu(g)*u rounded to BF16 when round_h != 0 (where a
+ * BF16 pipeline stores it), and optionally mag[r*width+c] = sum_p |h_p*wd[p][c]|
+ * + |x_c|, the magnitude of the down projection and residual sums. */
+void or_mlp_rows_ex(size_t width, size_t hidden, const float *x, const float *norm_weight,
+                    const float *wg, const float *wu, const float *wd, double eps,
+                    const int64_t *rows, size_t nrows, int round_h, double *out, double *mag,
+                    int threads);
 
 /* ir.rs:524-557: the reference's generated FP32 GEMM kernels accumulate each output
  * sequentially over p=0..k-1 with fmaf starting from 0.0f. Bit-exact restatement. */
@@ -48,6 +55,7 @@ typedef struct or_validation {
     size_t checked_elements, total_elements;
     double max_abs_error, max_scaled_error;
     int64_t first_bad_index;
+    double max_magnitude_error; /* max |out - expected| / sum|a*b| over the sample */
 } or_validation;
 int or_validation_check(size_t m, size_t n, size_t k, const float *a, const float *b,
                         const float *out, size_t budget, int fp16, double coef_override,
@@ -88,6 +96,11 @@ void or_attention(size_t bh, size_t seq, size_t dim, int causal, const float *q,
 void or_attention_rows(size_t seq, size_t dim, int causal, const float *q, const float *k,
                        const float *v, const int64_t *bh_idx, const int64_t *row_idx,
                        size_t npairs, double *out, int threads);
+/* The same rows plus mag[t*dim+d] = sum_col p[col]*|v[col][d]| (softmax weights p):
+ * the magnitude that scales the rounding error of the weighted sum. */
+void or_attention_rows_bound(size_t seq, size_t dim, int causal, const float *q, const float *k,
+                             const float *v, const int64_t *bh_idx, const int64_t *row_idx,
+                             size_t npairs, double *out, double *mag, int threads);
 
 /* workloads.rs:466-479: FP64 chain normalize -> gate/up dot -> g*sigmoid(g)*u ->
  * down dot -> +x for listed token rows. Weights row-major: wg, wu [width, hidden],

@@ -31,7 +31,7 @@ _sz = ctypes.c_size_t
 class Validation(ctypes.Structure):
     _fields_ = [("checked_elements", _sz), ("total_elements", _sz),
                 ("max_abs_error", ctypes.c_double), ("max_scaled_error", ctypes.c_double),
-                ("first_bad_index", ctypes.c_int64)]
+                ("first_bad_index", ctypes.c_int64), ("max_magnitude_error", ctypes.c_double)]
 
 
 class Check(ctypes.Structure):
@@ -75,6 +75,10 @@ def lib():
                                         _sz, _f64p, ctypes.c_int]
         L.or_mlp_rows.argtypes = [_sz, _sz, _f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_double,
                                   _i64p, _sz, _f64p, ctypes.c_int]
+        L.or_attention_rows_bound.argtypes = [_sz, _sz, ctypes.c_int, _f32p, _f32p, _f32p, _i64p, _i64p,
+                                              _sz, _f64p, _f64p, ctypes.c_int]
+        L.or_mlp_rows_ex.argtypes = [_sz, _sz, _f32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_double,
+                                     _i64p, _sz, ctypes.c_int, _f64p, _f64p, ctypes.c_int]
         L.or_f32_to_bf16.argtypes = [ctypes.c_float]
         L.or_f32_to_bf16.restype = ctypes.c_uint16
         L.or_bf16_to_f32.argtypes = [ctypes.c_uint16]
@@ -212,6 +216,44 @@ def attention_rows(seq, dim, causal, q, k, v, bh_idx, row_idx, threads=1):
     lib().or_attention_rows(seq, dim, int(causal), _c(q).ravel(), _c(k).ravel(), _c(v).ravel(),
                             bh_idx, row_idx, len(bh_idx), out, threads)
     return out.reshape(len(bh_idx), dim)
+
+
+def attention_rows_bound(seq, dim, causal, q, k, v, bh_idx, row_idx, threads=1):
+    """(reference rows, magnitude sum_j p_j*|v_j|) per output element, both
+    [len(bh_idx), dim]: the error of a weighted sum whose weights and output are
+    rounded to 2^-t relative is bounded by ~2^-t times the magnitude."""
+    bh_idx, row_idx = _c(bh_idx, np.int64), _c(row_idx, np.int64)
+    out = np.empty(len(bh_idx) * dim, np.float64)
+    mag = np.empty(len(bh_idx) * dim, np.float64)
+    lib().or_attention_rows_bound(seq, dim, int(causal), _c(q).ravel(), _c(k).ravel(), _c(v).ravel(),
+                                  bh_idx, row_idx, len(bh_idx), out, mag, threads)
+    return out.reshape(len(bh_idx), dim), mag.reshape(len(bh_idx), dim)
+
+
+def mlp_rows_bf16h(width, hidden, x, norm_weight, wg, wu, wd, eps, rows, threads=1):
+    """The MLP chain with h rounded to BF16 where the fused block stores it, and
+    the magnitude sum_p |h_p*wd_pc| + |x_c| of each output element."""
+    rows = _c(rows, np.int64)
+    out = np.empty(len(rows) * width, np.float64)
+    mag = np.empty(len(rows) * width, np.float64)
+    lib().or_mlp_rows_ex(width, hidden, _c(x).ravel(), _c(norm_weight).ravel(), _c(wg).ravel(),
+                         _c(wu).ravel(), _c(wd).ravel(), eps, rows, len(rows), 1, out, mag, threads)
+    return out.reshape(len(rows), width), mag.reshape(len(rows), width)
+
+
+def bounded_error(got, ref, mag, out_rel, coef):
+    """Checks |got - ref| <= out_rel*|ref| + coef*mag elementwise (the output's own
+    rounding plus a validation.rs-style bound on the sum). Returns (ok, max of
+    |got - ref| / mag, index of the first violation or -1)."""
+    got = np.asarray(got, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    mag = np.asarray(mag, np.float64).ravel()
+    if not (np.isfinite(got).all() and np.isfinite(ref).all()):
+        return False, float("inf"), int(np.argmin(np.isfinite(got) & np.isfinite(ref)))
+    err = np.abs(got - ref)
+    bad = err > out_rel * np.abs(ref) + coef * mag
+    scaled = float((err / np.maximum(mag, 1e-30)).max()) if err.size else 0.0
+    return (not bad.any()), scaled, int(np.argmax(bad)) if bad.any() else -1
 
 
 def mlp_rows(width, hidden, x, norm_weight, wg, wu, wd, eps, rows, threads=1):

@@ -4,10 +4,19 @@ Oracle: the reference's materialized FP64 attention (src/runtime/metal_lab.rs:33
 restated in oracle/oracle.c, evaluated on the same 16-bit inputs widened to FP64,
 on every row for small cases and on sampled rows at BASELINE sizes.
 
-Tolerance (written here, per element): |got - ref| <= atol + rtol*|ref| with
-atol = 4e-3 (P is rounded to the 16-bit input type before P.V, relative error
-2^-9 per weight; |V| <= ~5 for N(0,1) inputs) and rtol = 2^-8 for 16-bit outputs
-(one output rounding) or 1e-3 for FP32 outputs.
+Tolerance (written here, per output element), derived from where the kernels
+round: the softmax weights P are rounded to the input type before P.V (relative
+error <= u_in: 2^-8 for BF16, 2^-11 for FP16), so the weighted sum is off by at
+most u_in * m with m = sum_j p_j |v_j| (the oracle's magnitude, the attention
+analogue of validation.rs:35-91's sum|a*b|); 1e-4 * m more covers FP32
+accumulation and the exponential approximations (the FMA-pipe cubic is within
+7.5e-5 relative); a 16-bit output adds its own rounding, u_out * |ref|:
+
+    |got - ref| <= u_out * |ref| + (u_in + 1e-4) * m
+
+Each check returns the largest |got - ref| / m it saw; the tests print it so the
+achieved error can be read against north_star's 2e-3 (max relative error for
+BF16/TF32 inputs with FP32 accumulation).
 """
 import numpy as np
 import pytest
@@ -17,6 +26,9 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
+UNIT_ROUNDOFF = {"bf16": 2.0 ** -8, "fp16": 2.0 ** -11, "fp32": 0.0}
+ARITHMETIC = 1e-4
+
 
 @pytest.fixture(scope="module")
 def rt():
@@ -25,7 +37,9 @@ def rt():
     r.close()
 
 
-def run_attention(rt, B, H, S, D, causal, dtype="bf16", out_dtype=None, seed=0):
+def run_attention(rt, B, H, S, D, causal, dtype="bf16", out_dtype=None, seed=0, heads=None):
+    """Runs one attention launch; returns (O rows, Q, K, V) as FP32 arrays for the
+    heads listed in `heads` (all when None), in that order."""
     n = B * H * S * D
     q, k, v = (rt.alloc(n, dtype) for _ in range(3))
     for i, buf in enumerate((q, k, v)):
@@ -37,19 +51,27 @@ def run_attention(rt, B, H, S, D, causal, dtype="bf16", out_dtype=None, seed=0):
     kern = rt.compile(spec)
     assert kern.info["path"] == "tcgen05", kern.info
     rt.execute([(kern, [q, k, v, o])], repeats=2)
-    qf, kf, vf = (rt.download_f32(x) if dtype == "bf16" else rt.download(x).astype(np.float32) for x in (q, k, v))
-    got = rt.download_f32(o) if (out_dtype or dtype) == "bf16" else rt.download(o).astype(np.float32)
-    return got.reshape(B * H, S, D), qf, kf, vf
+    heads = list(range(B * H)) if heads is None else list(heads)
+
+    def fetch(buf):
+        parts = [rt.download_f32(buf, h * S * D, S * D) for h in heads]
+        return np.concatenate(parts).astype(np.float32)
+
+    got, qf, kf, vf = (fetch(x) for x in (o, q, k, v))
+    for x in (q, k, v, o):
+        x.free()
+    return got.reshape(len(heads), S, D), qf, kf, vf
 
 
-def check(got, qf, kf, vf, S, D, causal, pairs, out16):
+def check(got, qf, kf, vf, S, D, causal, pairs, dtype="bf16", out_dtype=None):
+    """pairs: (head index into the fetched heads, row) arrays. Returns the largest
+    |got - ref| / m over the checked elements."""
     bh, rows = pairs
-    ref = O.attention_rows(S, D, causal, qf, kf, vf, bh, rows, threads=O.max_threads())
+    ref, mag = O.attention_rows_bound(S, D, causal, qf, kf, vf, bh, rows, threads=O.max_threads())
     g = got[bh, rows]
-    rtol = 2 ** -8 if out16 else 1e-3
-    rc, r = O.compare(g.ravel(), ref.ravel(), 4e-3, rtol)
-    assert rc == 0, (r.first_bad_index, r.max_abs_error)
-    return np.abs(g - ref).max()
+    ok, scaled, bad = O.bounded_error(g, ref, mag, UNIT_ROUNDOFF[out_dtype or dtype], UNIT_ROUNDOFF[dtype] + ARITHMETIC)
+    assert ok, (bad, g.ravel()[bad], ref.ravel()[bad], mag.ravel()[bad])
+    return scaled
 
 
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
@@ -59,7 +81,7 @@ def test_attention_all_rows(rt, B, H, S, D, causal):
     got, qf, kf, vf = run_attention(rt, B, H, S, D, causal, seed=S + D)
     bh = np.repeat(np.arange(B * H), S)
     rows = np.tile(np.arange(S), B * H)
-    check(got, qf, kf, vf, S, D, causal, (bh, rows), True)
+    print(f"max |err|/m = {check(got, qf, kf, vf, S, D, causal, (bh, rows)):.2e}")
 
 
 @pytest.mark.parametrize("dtype,out_dtype", [("fp16", None), ("bf16", "fp32"), ("fp16", "fp32")])
@@ -68,7 +90,7 @@ def test_attention_dtypes(rt, dtype, out_dtype):
     got, qf, kf, vf = run_attention(rt, B, H, S, D, True, dtype, out_dtype, seed=3)
     bh = np.repeat(np.arange(B * H), S)
     rows = np.tile(np.arange(S), B * H)
-    check(got, qf, kf, vf, S, D, True, (bh, rows), (out_dtype or dtype) != "fp32")
+    print(f"max |err|/m = {check(got, qf, kf, vf, S, D, True, (bh, rows), dtype, out_dtype):.2e}")
 
 
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
@@ -79,7 +101,39 @@ def test_attention_baseline_config2_sampled(rt, causal):
     rng = np.random.default_rng(0)
     bh = rng.integers(0, B * H, 96)
     rows = np.concatenate([[0, 1, 127, 128, S - 1, S - 128], rng.integers(0, S, 90)])
-    check(got, qf, kf, vf, S, D, causal, (bh, rows), True)
+    print(f"max |err|/m = {check(got, qf, kf, vf, S, D, causal, (bh, rows)):.2e}")
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_attention_baseline_config2_fp32_out_error(rt, causal):
+    # The same workload with an FP32 output, so that only the kernel's own
+    # rounding (P in BF16) is measured: the largest |err|/m is north_star's
+    # "max relative error" in validation.rs form.
+    B, H, S, D = 4, 16, 2048, 128
+    got, qf, kf, vf = run_attention(rt, B, H, S, D, causal, out_dtype="fp32", seed=11)
+    rng = np.random.default_rng(1)
+    bh = rng.integers(0, B * H, 256)
+    rows = np.concatenate([np.arange(8), [127, 128, S - 1, S - 128], rng.integers(0, S, 244)])
+    scaled = check(got, qf, kf, vf, S, D, causal, (bh, rows), "bf16", "fp32")
+    print(f"C2 {'causal' if causal else 'full'} FP32 out: max |err|/m = {scaled:.2e} (P rounding bound 2^-8 = 3.9e-3)")
+
+
+# BASELINE config 5 attention (B=8, H=32, D=128, BF16) at S = 4096 / 8192 / 16384,
+# and non-causal at the same lengths: several persistent rounds of work items per
+# SM, head groups sized for L2, the last query and key tiles. Sampled heads are
+# fetched alone (each Q/K/V is up to 1 GiB at S=16384).
+@pytest.mark.parametrize("S", [4096, 8192, 16384])
+@pytest.mark.parametrize("causal", [True, False], ids=["causal", "full"])
+def test_attention_baseline_config5_sampled(rt, S, causal):
+    B, H, D = 8, 32, 128
+    rng = np.random.default_rng(S + causal)
+    heads = sorted({0, B * H - 1, *rng.integers(0, B * H, 6).tolist()})
+    got, qf, kf, vf = run_attention(rt, B, H, S, D, causal, seed=S // 1024, heads=heads)
+    nrow = 192
+    bh = rng.integers(0, len(heads), nrow)
+    rows = np.concatenate([[0, 1, 127, 128, 255, 256, S - 1, S - 2, S - 128, S - 129], rng.integers(0, S, nrow - 10)])
+    scaled = check(got, qf, kf, vf, S, D, causal, (bh, rows))
+    print(f"C5 S={S} {'causal' if causal else 'full'}: max |err|/m = {scaled:.2e}")
 
 
 @pytest.mark.parametrize("B,H,S,D,causal,out_dtype", [
@@ -95,7 +149,7 @@ def test_attention_persistent_items(rt, B, H, S, D, causal, out_dtype):
     rng = np.random.default_rng(S)
     bh = np.concatenate([[0, B * H - 1, B * H // 2], rng.integers(0, B * H, 93)])
     rows = np.concatenate([[0, S - 1, 127, 128 % S], rng.integers(0, S, 92)])
-    check(got, qf, kf, vf, S, D, causal, (bh, rows), out_dtype is None)
+    check(got, qf, kf, vf, S, D, causal, (bh, rows), "bf16", out_dtype)
 
 
 def test_attention_uniform_rows_kat(rt):
@@ -167,7 +221,7 @@ def test_attention_pair_kernel(rt, pair_kernel, B, H, S, causal):
     # both CTAs of a pair, tile edges, the last (partial) tile and random rows
     edges = [min(e, S - 1) for e in (0, 1, 127, 128, 255, 256, S - 1, S - 2, (S // 256) * 256, (S // 256) * 256 + 128)]
     rows = np.concatenate([edges, rng.integers(0, S, nrow - len(edges))])
-    check(got, qf, kf, vf, S, D, causal, (bh, rows), True)
+    print(f"max |err|/m = {check(got, qf, kf, vf, S, D, causal, (bh, rows)):.2e}")
 
 
 @pytest.mark.parametrize("dtype,out_dtype", [("fp16", None), ("bf16", "fp32")])
@@ -175,7 +229,7 @@ def test_attention_pair_kernel_dtypes(rt, pair_kernel, dtype, out_dtype):
     B, H, S, D = 1, 1, 2048, 128
     got, qf, kf, vf = run_attention(rt, B, H, S, D, False, dtype, out_dtype, seed=5)
     rows = np.arange(0, S, 3)
-    check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), (out_dtype or dtype) != "fp32")
+    check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), dtype, out_dtype)
 
 
 def test_attention_pair_kernel_rescales(rt, pair_kernel):
@@ -196,7 +250,7 @@ def test_attention_pair_kernel_rescales(rt, pair_kernel):
     got = rt.download_f32(bufs[3]).reshape(1, S, D)
     qf, kf, vf = (rt.download_f32(b) for b in bufs[:3])
     rows = np.arange(0, S, 7)
-    check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows), True)
+    check(got, qf, kf, vf, S, D, False, (np.zeros_like(rows), rows))
 
 
 def test_attention_pair_kernel_uniform_kat(rt, pair_kernel):

@@ -465,3 +465,23 @@ def test_reference_bridge_and_this_library_agree_on_abi1():
         L.jr_destroy(ctx)
         results.append(out)
     assert np.array_equal(results[0], results[1])
+
+
+def test_fp32_ffma_gemm_baseline_config1_bit_exact(rt):
+    # FP32 C = A.B, M = N = K = 512, A and B ~ U[-1,1] from seed
+    # 0, FP32 accumulation. The FFMA kernel sums the k products in order with one
+    # fmaf each, so it equals the sequential FP32 oracle bit for bit, and it is
+    # within validation.rs:35-91 of the FP64 oracle (north_star: <= 1e-5 relative).
+    m = n = k = 512
+    a, b = rt.alloc(m * k), rt.alloc(k * n)
+    rt.fill(a, "uniform", seed=0, stream=0, lo=-1.0, hi=1.0)
+    rt.fill(b, "uniform", seed=0, stream=1, lo=-1.0, hi=1.0)
+    out = rt.alloc(m * n)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True})
+    assert kern.info["path"] == "simt", kern.info
+    rt.execute([(kern, [a, b, out])])
+    af, bf, got = rt.download(a), rt.download(b), rt.download(out)
+    assert np.array_equal(got, O.gemm_fp32_sequential(m, n, k, af, bf, threads=O.max_threads()))
+    rc, v = O.validation_check(m, n, k, af, bf, got)
+    assert rc == 0 and v.max_scaled_error < 1
+    print(f"C1 FFMA 512^3: bit-exact to the sequential FP32 sum; max |err|/sum|a*b| vs FP64 = {v.max_magnitude_error:.2e}")

@@ -132,3 +132,39 @@ def test_unaligned_shapes_take_simt_path(rt):
     rt.execute([(kern, [a, b, out])])
     rc, v = O.validation_check(m, n, k, af, bf, rt.download(out))
     assert rc == 0
+
+
+# BASELINE configs 5 (square BF16 and TF32 GEMMs up to 16384^3) at full size:
+# several 128x256 tiles per persistent CTA, so both TMEM accumulators alternate,
+# the [K,N] and [N,K] B layouts, FP32 and BF16 outputs, and the TF32 [K,N]
+# transpose path. Checked on validation.rs:35-91's evenly spaced sample (16384
+# elements). 16-bit inputs: FP32 accumulation only, coef = 2*K*eps32; a BF16
+# output adds its rounding (<= 2^-8 |out| <= 2^-8 sum|a*b|) to the coefficient.
+# TF32 inputs: the reference's reduced-precision coefficient 0.0012.
+BIG = [("bf16", False, "fp32", 2048), ("bf16", True, "fp32", 2048), ("bf16", False, "bf16", 2048),
+       ("bf16", True, "bf16", 2048), ("bf16", False, "fp32", 8192), ("bf16", False, "bf16", 8192),
+       ("bf16", True, "fp32", 8192), ("bf16", True, "bf16", 8192), ("bf16", False, "fp32", 16384),
+       ("tf32", False, "fp32", 2048), ("tf32", False, "fp32", 4096), ("tf32", True, "fp32", 4096),
+       ("tf32", False, "fp32", 8192)]
+
+
+@pytest.mark.parametrize("dtype,b_nk,out_dtype,size", BIG, ids=lambda v: str(v))
+def test_tc_gemm_baseline_sizes_sampled(rt, dtype, b_nk, out_dtype, size):
+    m = n = k = size
+    a, b, af, bf = operands(rt, m, n, k, dtype, b_nk, seed=size + (7 if b_nk else 0))
+    out = rt.alloc(m * n, out_dtype)
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": dtype,
+                       "b_layout": "nk" if b_nk else "kn", "out_dtype": out_dtype})
+    assert kern.info["path"] == "tcgen05", kern.info
+    rt.execute([(kern, [a, b, out])], repeats=2)
+    got = rt.download_f32(out)
+    if dtype == "tf32":
+        coef = 0.0012
+    else:
+        coef = 2 * k * 2.0 ** -23 + (2.0 ** -8 if out_dtype == "bf16" else 0.0)
+    rc, v = O.validation_check(m, n, k, af, bf, got, budget=1 << 14, coef=coef)
+    assert rc == 0, (rc, v.first_bad_index, v.max_scaled_error, kern.info["impl"])
+    print(f"{kern.info['impl']} {size}^3: max |err|/sum|a*b| = {v.max_magnitude_error:.2e}, "
+          f"max err/tolerance = {v.max_scaled_error:.3f}")
+    for x in (a, b, out):
+        x.free()

@@ -5,10 +5,16 @@
    workloads.rs:390-481 (xorshift32 inputs, compare at 5e-5/5e-5).
 2. The fused BF16 block (rms_inv -> tcgen05 GEMM with row-scale + SwiGLU
    epilogue -> tcgen05 GEMM with residual epilogue), against the FP64 chain
-   evaluated on the same effective BF16 weights. Tolerance: h and y are stored
-   in BF16 (2^-8 relative each), so |err| <= 2e-2*rms(y) + 2^-7*|y|.
+   evaluated on the same effective BF16 weights, with h rounded to BF16 where the
+   block stores it (oracle or_mlp_rows_ex). Tolerance, from where the block
+   rounds: y is stored in BF16 (2^-8 relative), and the remaining error is FP32
+   accumulation plus rare one-ulp differences in the BF16 h, bounded by 2e-5
+   times m = sum_p |h_p * Wd[p][c]| + |x_c| (validation.rs:35-91's sum|a*b|
+   form): |got - ref| <= 2^-8 |ref| + 2e-5 m. The tests print the largest
+   |got - ref| / m.
 3. Tensor-parallel sharding math on one GPU: the shards' partial outputs sum to
-   the unsharded block (the all-reduce itself is covered by the multi-GPU test).
+   the unsharded block (the all-reduce itself is covered by the multi-GPU test);
+   each BF16 partial adds its own rounding, 2^-8 |partial|.
 """
 import math
 
@@ -66,7 +72,8 @@ def test_reference_six_op_fp32_mlp(rt, batch, width, hidden):
 
 
 def effective_oracle(rt, mlp_shards, rows):
-    """FP64 chain on the weights the device actually holds (BF16, norm folded)."""
+    """FP64 chain on the weights the device actually holds (BF16, norm folded),
+    h rounded to BF16; returns (reference rows, magnitude m)."""
     d = mlp_shards[0].d
     x = rt.download_f32(mlp_shards[0].x)
     wg_parts, wu_parts, wd_parts = [], [], []
@@ -79,13 +86,21 @@ def effective_oracle(rt, mlp_shards, rows):
     wu = np.concatenate(wu_parts, axis=1)
     wd = np.concatenate(wd_parts, axis=0)
     ffn = wg.shape[1]
-    return O.mlp_rows(d, ffn, x, np.ones(d, np.float32), wg, wu, wd, mlp_shards[0].eps, rows, threads=O.max_threads())
+    return O.mlp_rows_bf16h(d, ffn, x, np.ones(d, np.float32), wg, wu, wd, mlp_shards[0].eps, rows,
+                            threads=O.max_threads())
 
 
-def check_mlp(got_rows, ref):
-    scale = np.sqrt((ref ** 2).mean())
-    rc, r = O.compare(got_rows.ravel(), ref.ravel(), 2e-2 * scale, 2 ** -7)
-    assert rc == 0, (r.first_bad_index, r.max_abs_error, scale)
+ACCUMULATION = 2e-5
+
+
+def check_mlp(got_rows, oracle, out_rel=2.0 ** -8, extra=None):
+    ref, mag = oracle
+    if extra is not None:  # per-element rounding already in got (summed BF16 partials)
+        mag = mag + extra / ACCUMULATION
+    ok, scaled, bad = O.bounded_error(got_rows, ref, mag, out_rel, ACCUMULATION)
+    assert ok, (bad, got_rows.ravel()[bad], ref.ravel()[bad], mag.ravel()[bad])
+    print(f"max |err|/m = {scaled:.2e}")
+    return scaled
 
 
 @pytest.mark.parametrize("T,d,ffn", [(256, 256, 512), (200, 384, 1024)])
@@ -124,8 +139,13 @@ def test_tensor_parallel_shards_sum_to_block(rt):
     wd = (rng.standard_normal((ffn, d)) * 0.05).astype(np.float32)
     shards = [ResidualMLP(rt, T, d, ffn, tp=tp, rank=r, collective=False) for r in range(tp)]
     total = np.zeros(T * d, np.float64)
+    partial_size = np.zeros(T * d, np.float64)
     for s in shards:
         s.load(x, norm, wg, wu, wd)
         rt.execute(s.jobs())
-        total += rt.download_f32(s.y)
-    check_mlp(total.reshape(T, d), effective_oracle(rt, shards, np.arange(T)))
+        part = rt.download_f32(s.y).astype(np.float64)
+        total += part
+        partial_size += np.abs(part)
+    # each partial is rounded to BF16 once: 2^-8 |partial| per shard, no output rounding
+    check_mlp(total.reshape(T, d), effective_oracle(rt, shards, np.arange(T)), out_rel=0.0,
+              extra=(2.0 ** -8 * partial_size).reshape(T, d))
