@@ -14,11 +14,19 @@ Contract (one JSON line on rank 0):
              measured dense BF16 peak; traffic from the committed ncu summary.
   cpu_baseline  the FP64 oracle (the reference's CPU attention restated,
              metal_lab.rs:33-73) on a bounded sample of rows, all host threads.
-  components the row kernels and the lowered IR expression (
-             each with the SM clocks of its own timed region), GEMM 8192^3 BF16
-             split by output columns over the ranks, the residual MLP block
-             (tensor parallel with one NCCL all-reduce),
-             non-causal attention.
+  components every other BASELINE configuration, each with its roofline and
+             the SM clocks of its own timed region: the row kernels and the
+             lowered IR expression (config 3); non-causal attention (config 2);
+             causal attention B=8 H=32 D=128 at S=4096/8192/16384 split by
+             batch x head over the ranks (config 5, strong scaling: a fixed
+             problem); the FP32 FFMA GEMM 512^3 (config 1); GEMM 8192^3 BF16 and
+             the BF16/TF32 square GEMMs 1024^3..16384^3 split by output columns
+             (config 5); the residual MLP block (config 4, tensor parallel with
+             one NCCL all-reduce).
+  max_err    correctness evidence of this run, taken outside the timed regions
+             on rank 0: sampled rows of the headline attention and of the MLP
+             block against the FP64 oracle (max |err| / m, m the magnitude of
+             the rounded sums: sum_j p_j |v_j| and sum_p |h_p Wd_pc| + |x_c|).
 Multi-GPU: one process per GPU (torchrun); each rank runs its own batch x head
 shard of the headline attention (weak scaling, no collective on the data path).
 
@@ -209,7 +217,15 @@ def attention_bench(rt, jc, steps, warmup, causal, batch):
     return jobs, attn, (q, k, v, o), flush_buf
 
 
-def gemm_bench(rt, dist, world, steps, warmup, m=8192):
+def tensor_roofline(achieved_per_gpu, peaks, which):
+    """Tensor-bound roofline of one GPU's share against the measured BF16 peak
+    ("bf16" = burst, for a kernel timed alone; "bf16_sustained" inside a long step)."""
+    return {"bound": "tensor", "achieved": achieved_per_gpu, "peak": peaks[which], "unit": "TFLOP/s",
+            "frac": achieved_per_gpu / peaks[which],
+            "peak_source": peaks["source"] + (" burst bf16" if which == "bf16" else " sustained bf16")}
+
+
+def gemm_bench(rt, dist, world, steps, warmup, peaks, device=0, m=8192):
     """One m^3 BF16 GEMM split by output columns over the ranks (strong scaling):
     rank r computes C[:, cols_r] = A . B[:, cols_r] with B stored [N, K] per shard."""
     from jade_compute_b200 import parallel
@@ -224,14 +240,16 @@ def gemm_bench(rt, dist, world, steps, warmup, m=8192):
                     "b_layout": layout})
     rt.execute([(g, [a, b, c])], repeats=max(warmup, 3))
     barrier(dist)
-    t = rt.execute([(g, [a, b, c])], repeats=steps, per_job=True)
+    with ClockSampler(device) as clk:
+        t = rt.execute([(g, [a, b, c])], repeats=steps, per_job=True)
     ms = reduce_max(dist, t.job_ms[0] / steps)
     tflops = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
     for x in (a, b, c):
         x.free()
     return {"workload": f"GEMM {m}^3 BF16 in, FP32 accumulate, BF16 out (BASELINE configs[4]), N-column shards",
             "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
-            "impl": g.info.get("impl")}
+            "impl": g.info.get("impl"), "roofline": tensor_roofline(tflops / world, peaks, "bf16"),
+            "clocks": clk.summary()}
 
 
 def row_benches(rt, steps, warmup, peaks, device=0):
@@ -287,7 +305,7 @@ def row_benches(rt, steps, warmup, peaks, device=0):
     return out
 
 
-def mlp_bench(rt, dist, world, steps, warmup, peaks):
+def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     """T=8192, d=4096, ffn=14336 residual MLP, tensor parallel
     over the ranks with one NCCL all-reduce after the down projection."""
     from jade_compute_b200 import parallel
@@ -301,7 +319,8 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks):
     jobs = mlp.jobs()
     rt.execute(jobs, repeats=max(warmup, 3))
     barrier(dist)
-    t = rt.execute(jobs, repeats=steps, per_job=True)
+    with ClockSampler(rt.device) as clk:
+        t = rt.execute(jobs, repeats=steps, per_job=True)
     ms = reduce_max(dist, t.gpu_ms / steps)
     flops = 6.0 * T * d * ffn
     per_gpu_tflops = flops / world / (ms * 1e-3) / 1e12
@@ -310,42 +329,55 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks):
            "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": [x / steps for x in t.job_ms],
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
-           "kernels": [k.info.get("impl") for k, _ in jobs]}
+           "kernels": [k.info.get("impl") for k, _ in jobs], "clocks": clk.summary()}
+    if check:
+        out["max_err"] = mlp_error(rt, mlp, world, seed=11)
     if world > 1:
         rt.comm_destroy()
     return out
 
 
-def sweep(rt, dist, world, rank, steps, warmup, peaks, device=0):
-    """BASELINE config 5 on this box: BF16 and TF32 square GEMMs M=N=K in
-    {1k..16k} split by output columns over the ranks, and causal attention B=8,
-    H=32, D=128, S in {4k, 8k, 16k} split by batch x head (B*H/world heads per rank)."""
+def c5_attention(rt, dist, world, rank, steps, warmup, peaks, device=0, seqs=(4096, 8192, 16384), causal=True):
+    """BASELINE config 5 attention: B=8, H=32, D=128, BF16, S in {4k, 8k, 16k},
+    one fixed problem split by batch x head over the ranks (B*H/world heads per
+    rank: strong scaling). Value = FLOPs of the whole problem / the slowest rank's
+    mean launch time."""
     from jade_compute_b200 import parallel
     out = []
-    # attention first: after the long GEMMs (power-capped) the SM clock recovers slowly
     Bs, Hs = 8, 32
-    for seq in (4096, 8192, 16384):
+    for seq in seqs:
         heads = parallel.split_range(Bs * Hs, world, rank)
         nh = len(heads)
         n = nh * seq * D
         q, k, v, o = (rt.alloc(n, "bf16") for _ in range(4))
         for i, buf in enumerate((q, k, v)):
             rt.fill(buf, "normal", seed=8, stream=i + 4 * rank, lo=0.0, hi=1.0)
-        attn = rt.compile({"op": "attention_online", "heads": nh, "seq": seq, "dim": D, "causal": True, "dtype": "bf16"})
+        attn = rt.compile({"op": "attention_online", "heads": nh, "seq": seq, "dim": D, "causal": causal, "dtype": "bf16"})
         rt.execute([(attn, [q, k, v, o])], repeats=max(warmup, 2))
         barrier(dist)
         reps = max(3, min(steps, 20))
         with ClockSampler(device) as clk:
             t = rt.execute([(attn, [q, k, v, o])], repeats=reps, per_job=True)
         ms = reduce_max(dist, t.job_ms[0] / reps)
-        tf = causal_flops(Bs, Hs, seq, D) / (ms * 1e-3) / 1e12
-        out.append({"workload": f"causal attention B={Bs} H={Hs} S={seq} D={D} BF16, batch x head split x{world}",
-                    "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"],
-                    "impl": attn.info.get("impl"), "clocks": clk.summary()})
+        flops = causal_flops(Bs, Hs, seq, D) if causal else full_flops(Bs, Hs, seq, D)
+        tf = flops / (ms * 1e-3) / 1e12
+        out.append({"workload": f"{'causal' if causal else 'non-causal'} attention B={Bs} H={Hs} S={seq} D={D} BF16 "
+                                f"(BASELINE configs[4]), batch x head split x{world}",
+                    "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
+                    "roofline": tensor_roofline(tf / world, peaks, "bf16"), "impl": attn.info.get("impl"),
+                    "clocks": clk.summary()})
         for x in (q, k, v, o):
             x.free()
+    return out
+
+
+def c5_gemms(rt, dist, world, rank, steps, warmup, peaks, device=0, sizes=(1024, 2048, 4096, 8192, 16384)):
+    """BASELINE config 5 GEMMs: BF16 and TF32 square M=N=K, inputs U[-1,1], FP32
+    out, B and C split by output columns over the ranks (strong scaling)."""
+    from jade_compute_b200 import parallel
+    out = []
     for dtype in ("bf16", "tf32"):
-        for m in (1024, 2048, 4096, 8192, 16384):
+        for m in sizes:
             cols = parallel.split_range(m, world, rank)
             n = len(cols)
             a, b, c = rt.alloc(m * m, dtype), rt.alloc(n * m, dtype), rt.alloc(m * n, "fp32")
@@ -359,12 +391,92 @@ def sweep(rt, dist, world, rank, steps, warmup, peaks, device=0):
                 t = rt.execute([(g, [a, b, c])], repeats=reps, per_job=True)
             ms = reduce_max(dist, t.job_ms[0] / reps)
             tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
-            out.append({"workload": f"GEMM {m}^3 {dtype} (FP32 out), N-split x{world}", "value": tf, "unit": "TFLOP/s",
-                        "ms_per_step": ms, "frac_of_bf16_peak_per_gpu": tf / world / peaks["bf16"], "impl": g.info.get("impl"),
+            out.append({"workload": f"GEMM {m}^3 {dtype} (FP32 out, BASELINE configs[4]), N-split x{world}",
+                        "value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
+                        "roofline": tensor_roofline(tf / world, peaks, "bf16"), "impl": g.info.get("impl"),
                         "clocks": clk.summary()})
             for x in (a, b, c):
                 x.free()
     return out
+
+
+def sweep(rt, dist, world, rank, steps, warmup, peaks, device=0):
+    """BASELINE config 5 on this box: attention first (after the long
+    power-capped GEMMs the SM clock recovers slowly), then the GEMMs."""
+    return (c5_attention(rt, dist, world, rank, steps, warmup, peaks, device)
+            + c5_gemms(rt, dist, world, rank, steps, warmup, peaks, device))
+
+
+def ffma_bench(rt, steps, warmup, device=0):
+    """FP32 GEMM 512^3, A and B ~ U[-1,1] from seed 0, FP32
+    FFMA accumulation in k order (bit-exact to the sequential FP32 sum), L2
+    flushed between launches. Roofline: the FP32 FFMA peak, SMs x 128 lanes x 2
+    FLOP x the maximum SM clock (nominal: no measured FP32 peak exists)."""
+    m = 512
+    a, b, c = rt.alloc(m * m), rt.alloc(m * m), rt.alloc(m * m)
+    rt.fill(a, "uniform", seed=0, stream=0, lo=-1, hi=1)
+    rt.fill(b, "uniform", seed=0, stream=1, lo=-1, hi=1)
+    flush_buf = rt.alloc_bytes(256 << 20)
+    flush = rt.compile({"op": "l2_flush", "bytes": 256 << 20})
+    g = rt.compile({"op": "gemm", "m": m, "n": m, "k": m, "tiled": True})
+    jobs = [(flush, [flush_buf]), (g, [a, b, c])]
+    rt.execute(jobs, repeats=max(warmup, 3))
+    reps = max(10, min(steps, 100))
+    with ClockSampler(device) as clk:
+        t = rt.execute(jobs, repeats=reps, per_job=True)
+    ms = t.job_ms[1] / reps
+    tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
+    try:
+        import torch
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+    except Exception:
+        sms = 148
+    max_mhz = clk.max_mhz or 1965.0
+    peak = sms * 128 * 2 * max_mhz * 1e6 / 1e12
+    for x in (a, b, c, flush_buf):
+        x.free()
+    return {"workload": "FP32 GEMM 512^3 FFMA, k-ordered FP32 accumulation (BASELINE configs[0])", "value": tf,
+            "unit": "TFLOP/s", "ms_per_step": ms, "impl": g.info.get("impl"),
+            "roofline": {"bound": "ffma", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "peak_source": f"nominal FP32 FFMA: {sms} SMs x 128 lanes x 2 FLOP x {max_mhz:.0f} MHz"},
+            "reference_published_ms": 0.1169, "clocks": clk.summary()}
+
+
+def attention_error(rt, bufs, batch_heads, causal, seed=0, nrows=48):
+    """Max |err| / m of sampled rows of an attention output against the FP64
+    oracle (m = sum_j p_j |v_j|), outside any timed region."""
+    from oracle import oracle as O
+    q, k, v, o = bufs
+    rng = np.random.default_rng(seed)
+    heads = sorted({0, batch_heads - 1, int(rng.integers(0, batch_heads))})
+    fetch = lambda buf: np.concatenate([rt.download_f32(buf, h * S * D, S * D) for h in heads])
+    qf, kf, vf, got = (fetch(x) for x in (q, k, v, o))
+    bh = rng.integers(0, len(heads), nrows)
+    rows = np.concatenate([[0, 1, S - 1], rng.integers(0, S, nrows - 3)])
+    ref, mag = O.attention_rows_bound(S, D, causal, qf, kf, vf, bh, rows, threads=host_threads())
+    g = got.reshape(len(heads), S, D)[bh, rows]
+    ok, scaled, _ = O.bounded_error(g, ref, mag, 2.0 ** -8, 2.0 ** -8 + 1e-4)
+    return {"rows": int(nrows), "max_err_over_m": scaled, "within_bound": bool(ok),
+            "bound": "|err| <= 2^-8 |ref| + (2^-8 + 1e-4) m"}
+
+
+def mlp_error(rt, mlp, world, seed, rows=(0, 1, 4097, 8191)):
+    """Max |err| / m of sampled rows of the (all-reduced) MLP output against the
+    FP64 chain on the BF16 weights of every shard, h rounded to BF16 as stored
+    (m = sum_p |h_p Wd_pc| + |x_c|), outside any timed region."""
+    from oracle import oracle as O
+    from jade_compute_b200.mlp import synthetic_weights
+    rows = np.array(rows, np.int64)
+    wg, wu, wd = synthetic_weights(rt, mlp.d, mlp.ffn, world, seed)
+    x = rt.download_f32(mlp.x)
+    ref, mag = O.mlp_rows_bf16h(mlp.d, mlp.ffn, x, np.ones(mlp.d, np.float32), wg, wu, wd, mlp.eps, rows,
+                                threads=host_threads())
+    got = np.stack([rt.download_f32(mlp.y, int(r) * mlp.d, mlp.d) for r in rows])
+    err = np.abs(got - ref)
+    rms = float(np.sqrt((ref ** 2).mean()))
+    return {"rows": len(rows), "max_err_over_m": float((err / mag).max()), "max_err_over_rms": float(err.max() / rms),
+            "max_err_over_ref_bf16_ulps": float((err / np.maximum(np.abs(ref), rms * 1e-3)).max() / 2.0 ** -8),
+            "tp": world, "allreduce_dtype": "bf16"}
 
 
 def run_only(args):
@@ -383,7 +495,9 @@ def run_only(args):
             f = causal_flops(B, H, S, D) if w == "attention" else full_flops(B, H, S, D)
             res = {"workload": w, "value": f / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "impl": attn.info.get("impl")}
         elif w == "gemm":
-            res = gemm_bench(rt, dist, world, args.steps, args.warmup)
+            res = gemm_bench(rt, dist, world, args.steps, args.warmup, peaks, local)
+        elif w == "ffma":
+            res = ffma_bench(rt, args.steps, args.warmup, local)
         elif w == "mlp":
             res = mlp_bench(rt, dist, world, args.steps, args.warmup, peaks)
         elif w == "rows":
@@ -435,20 +549,31 @@ def run_ours(args):
         e2e_ms = reduce_max(dist, te.gpu_ms) / e2e_steps
         e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
         components = []
+        max_err = {"attention_c2": attention_error(rt, (q, k, v, o), B * H, True, seed=rank)}
         if not args.quick:
-            # row kernels and non-causal attention before the ~1 kW GEMM and MLP: measured
-            # right after those, they ran 10-28% slower (partly issue-bound, they follow
-            # the SM clock); each of them records the clocks of its own timed region
+            # light components first: measured right after the ~1 kW GEMMs and MLP they
+            # ran 10-28% slower (partly issue-bound, they follow the SM clock); each
+            # records the clocks of its own timed region
             components.extend(row_benches(rt, max(5, min(args.steps, 20)), args.warmup, peaks, local))
             jobs_f, attn_f, bufs_f, fb = attention_bench(rt, jc, args.steps, args.warmup, False, B)
+            reps_f = max(5, min(args.steps, 50))
             with ClockSampler(local) as clk_f:
-                tf = rt.execute(jobs_f, repeats=max(5, min(args.steps, 50)), per_job=True)
-            ms_f = tf.job_ms[1] / max(5, min(args.steps, 50))
-            components.append({"workload": f"non-causal attention B={B} H={H} S={S} D={D} BF16", "unit": "TFLOP/s",
-                               "value": full_flops(B, H, S, D) / (ms_f * 1e-3) / 1e12, "ms_per_step": ms_f,
-                               "impl": attn_f.info.get("impl"), "clocks": clk_f.summary()})
-            components.append(gemm_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup))
-            components.append(mlp_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks))
+                tf = rt.execute(jobs_f, repeats=reps_f, per_job=True)
+            ms_f = tf.job_ms[1] / reps_f
+            tf_f = full_flops(B, H, S, D) / (ms_f * 1e-3) / 1e12
+            components.append({"workload": f"non-causal attention B={B} H={H} S={S} D={D} BF16 (BASELINE configs[1])",
+                               "unit": "TFLOP/s", "value": tf_f, "ms_per_step": ms_f, "impl": attn_f.info.get("impl"),
+                               "roofline": tensor_roofline(tf_f, peaks, "bf16"), "clocks": clk_f.summary()})
+            for x in (*bufs_f, fb):
+                x.free()
+            components.extend(c5_attention(rt, dist, world, rank, args.steps, args.warmup, peaks, local))
+            components.append(ffma_bench(rt, args.steps, args.warmup, local))
+            components.append(gemm_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks, local))
+            components.extend(c5_gemms(rt, dist, world, rank, args.steps, args.warmup, peaks, local))
+            mlp = mlp_bench(rt, dist, world, max(5, min(args.steps, 20)), args.warmup, peaks, check=(rank == 0))
+            if "max_err" in mlp:
+                max_err["mlp_c4"] = mlp.pop("max_err")
+            components.append(mlp)
         cpu = None
         if rank == 0 and not args.no_cpu:
             from oracle import oracle as O
@@ -476,6 +601,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "region_ms": region_ms,
             "components": components,
+            "max_err": max_err,
         }
         if rank == 0:
             emit_line(line)
@@ -516,7 +642,7 @@ def _main(out_fd):
     ap.add_argument("--quick", action="store_true", help="headline only, no components")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "mlp", "rows", "sweep"], default=None,
+    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "ffma", "mlp", "rows", "sweep"], default=None,
                     help="run one workload alone (profiling), printing its own measurement")
     args = ap.parse_args()
     if args.warmup < 3:

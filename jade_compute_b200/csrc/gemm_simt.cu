@@ -6,15 +6,19 @@
 // accumulated as acc = fmaf(a[row,p], b[p,col], acc) for p = 0..K-1 in order,
 // starting from 0, which is exactly what the reference kernels compute, so FP32
 // results are bit-identical to them (and to the CPU restatement
-// or_gemm_fp32_sequential). Tiling: 128x128 block tile, K-step 8, 256 threads,
-// 8x8 outputs per thread held in registers, shared-memory double buffering.
+// or_gemm_fp32_sequential). Tiling: BM x BN block tile, K-step 8, each thread
+// holding TM x TN outputs in registers, shared-memory double buffering. Two
+// shapes: 128x128 tiles of 8x8 per thread (256 threads) when the output has at
+// least one tile per SM, else 32x64 tiles of 4x4 per thread (128 threads), which
+// spread a small GEMM (512^3: 128 blocks instead of 16) over the SMs; the k
+// order of every sum is the same in both.
 #include "common.cuh"
 #include "internal.hpp"
 
 namespace jade {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 8, kThreads = 256;
+constexpr int BK = 8;
 
 template <typename TA> __device__ __forceinline__ float load_op(const TA *p, bool tf32);
 template <> __device__ __forceinline__ float load_op<float>(const float *p, bool tf32) {
@@ -29,32 +33,42 @@ template <> __device__ __forceinline__ float load_op<float>(const float *p, bool
 template <> __device__ __forceinline__ float load_op<__nv_bfloat16>(const __nv_bfloat16 *p, bool) { return __bfloat162float(*p); }
 template <> __device__ __forceinline__ float load_op<__half>(const __half *p, bool) { return __half2float(*p); }
 
-// C[M,N] = A[M,K] * B   (B is [K,N] row-major, or [N,K] when kBnk)
-template <typename TA, typename TO, bool kBnk>
-__global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(const TA *__restrict__ A, const TA *__restrict__ B, TO *__restrict__ C,
-                                                             int M, int N, int K, bool tf32, const float *__restrict__ row_scale,
-                                                             const TO *__restrict__ residual) {
+// C[M,N] = A[M,K] * B   (B is [K,N] row-major, or [N,K] when kBnk). Thread
+// (tx, ty) owns TM/4 groups of 4 rows, group g at row ty*4 + g*BM/(TM/4), and
+// likewise TN/4 groups of 4 columns, so each k step reads its operands from
+// shared memory as conflict-free float4s.
+template <typename TA, typename TO, bool kBnk, int BM, int BN, int TM, int TN>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    gemm_ffma_kernel(const TA *__restrict__ A, const TA *__restrict__ B, TO *__restrict__ C, int M, int N, int K, bool tf32,
+                     const float *__restrict__ row_scale, const TO *__restrict__ residual) {
+    constexpr int kThreads = (BM / TM) * (BN / TN);
+    constexpr int kLoadsA = BM * BK / kThreads, kLoadsB = BN * BK / kThreads;
+    constexpr int kGroupsM = TM / 4, kGroupsN = TN / 4;
+    constexpr int kRowStride = BM / kGroupsM, kColStride = BN / kGroupsN;
+    static_assert(kLoadsA * kThreads == BM * BK && kLoadsB * kThreads == BN * BK, "tile loads must divide evenly");
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
     const int t = threadIdx.x;
-    const int tx = t % 16, ty = t / 16;
+    const int tx = t % (BN / TN), ty = t / (BN / TN);
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    float acc[8][8];
+    float acc[TM][TN];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
 
-    float ra[4], rb[4];
+    float ra[kLoadsA], rb[kLoadsB];
     auto gload = [&](int k0) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < kLoadsA; ++i) {  // A element (r, kk): consecutive threads walk k within a row
             const int idx = t + kThreads * i;
-            {  // A element (r, kk): consecutive threads walk k within a row
-                const int r = idx / BK, kk = idx % BK;
-                const int gr = m0 + r, gk = k0 + kk;
-                ra[i] = (gr < M && gk < K) ? load_op(A + (size_t)gr * K + gk, tf32) : 0.0f;
-            }
+            const int r = idx / BK, kk = idx % BK;
+            const int gr = m0 + r, gk = k0 + kk;
+            ra[i] = (gr < M && gk < K) ? load_op(A + (size_t)gr * K + gk, tf32) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kLoadsB; ++i) {
+            const int idx = t + kThreads * i;
             if (!kBnk) {  // B element (kk, c): consecutive threads walk columns
                 const int kk = idx / BN, c = idx % BN;
                 const int gk = k0 + kk, gc = n0 + c;
@@ -68,9 +82,13 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(const TA *__restric
     };
     auto sstore = [&](int buf) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < kLoadsA; ++i) {
             const int idx = t + kThreads * i;
             As[buf][idx % BK][idx / BK] = ra[i];
+        }
+#pragma unroll
+        for (int i = 0; i < kLoadsB; ++i) {
+            const int idx = t + kThreads * i;
             if (!kBnk) Bs[buf][idx / BN][idx % BN] = rb[i];
             else Bs[buf][idx % BK][idx / BK] = rb[i];
         }
@@ -85,17 +103,21 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(const TA *__restric
         if (kt + 1 < ktiles) gload((kt + 1) * BK);
 #pragma unroll
         for (int kk = 0; kk < BK; ++kk) {
-            float a[8], b[8];
-            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
-            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);
-            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][tx * 4]);
-            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 + tx * 4]);
-            a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
-            b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+            float a[TM], b[TN];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int g = 0; g < kGroupsM; ++g) {
+                const float4 v = *reinterpret_cast<const float4 *>(&As[buf][kk][g * kRowStride + ty * 4]);
+                a[4 * g] = v.x; a[4 * g + 1] = v.y; a[4 * g + 2] = v.z; a[4 * g + 3] = v.w;
+            }
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+            for (int g = 0; g < kGroupsN; ++g) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][kk][g * kColStride + tx * 4]);
+                b[4 * g] = v.x; b[4 * g + 1] = v.y; b[4 * g + 2] = v.z; b[4 * g + 3] = v.w;
+            }
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
         }
         if (kt + 1 < ktiles) {
             sstore(buf ^ 1);
@@ -103,13 +125,13 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(const TA *__restric
         }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int r = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    for (int i = 0; i < TM; ++i) {
+        const int r = m0 + (i / 4) * kRowStride + ty * 4 + (i % 4);
         if (r >= M) continue;
         const float sc = row_scale ? row_scale[r] : 1.0f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int c = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+        for (int j = 0; j < TN; ++j) {
+            const int c = n0 + (j / 4) * kColStride + tx * 4 + (j % 4);
             if (c >= N) continue;
             float v = row_scale ? acc[i][j] * sc : acc[i][j];
             if (residual) v += to_f32(residual[(size_t)r * N + c]);
@@ -118,10 +140,11 @@ __global__ void __launch_bounds__(kThreads) gemm_ffma_kernel(const TA *__restric
     }
 }
 
-template <typename TA, typename TO>
-LaunchFn ffma_launch(const Spec &s, bool tf32) {
+template <typename TA, typename TO, int BM, int BN, int TM, int TN>
+LaunchFn ffma_launch_tiles(const Spec &s, bool tf32) {
     const int M = (int)s.m, N = (int)s.n, K = (int)s.k;
     const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    constexpr int threads = (BM / TM) * (BN / TN);
     const bool bnk = s.b_nk, rs = s.row_scale, res = s.epilogue == "residual";
     return [=](cudaStream_t st, void **b) {
         int idx = 2;
@@ -129,25 +152,42 @@ LaunchFn ffma_launch(const Spec &s, bool tf32) {
         const TO *residual = res ? static_cast<const TO *>(b[idx++]) : nullptr;
         TO *out = static_cast<TO *>(b[idx]);
         if (bnk)
-            gemm_ffma_kernel<TA, TO, true><<<grid, kThreads, 0, st>>>((const TA *)b[0], (const TA *)b[1], out, M, N, K, tf32, row_scale, residual);
+            gemm_ffma_kernel<TA, TO, true, BM, BN, TM, TN>
+                <<<grid, threads, 0, st>>>((const TA *)b[0], (const TA *)b[1], out, M, N, K, tf32, row_scale, residual);
         else
-            gemm_ffma_kernel<TA, TO, false><<<grid, kThreads, 0, st>>>((const TA *)b[0], (const TA *)b[1], out, M, N, K, tf32, row_scale, residual);
+            gemm_ffma_kernel<TA, TO, false, BM, BN, TM, TN>
+                <<<grid, threads, 0, st>>>((const TA *)b[0], (const TA *)b[1], out, M, N, K, tf32, row_scale, residual);
         return cudaGetLastError();
     };
 }
 
+// 128x128 tiles when there is at least one per SM, else 32x64 tiles.
+template <typename TA, typename TO>
+LaunchFn ffma_launch(const Spec &s, bool tf32, int sm_count, std::string &impl) {
+    const long long big_tiles = (long long)((s.m + 127) / 128) * ((s.n + 127) / 128);
+    if (big_tiles >= sm_count) {
+        impl += "_128x128";
+        return ffma_launch_tiles<TA, TO, 128, 128, 8, 8>(s, tf32);
+    }
+    impl += "_32x64";
+    return ffma_launch_tiles<TA, TO, 32, 64, 4, 4>(s, tf32);
+}
+
 }  // namespace
 
-LaunchFn make_gemm_simt(Context *, const Spec &s, std::string &impl) {
+LaunchFn make_gemm_simt(Context *ctx, const Spec &s, std::string &impl) {
     if (s.epilogue == "swiglu") throw IrError("swiglu epilogue needs the tcgen05 path (K a multiple of 8)");
-    impl = std::string("gemm_ffma_128x128_") + dtype_name(s.dtype) + (s.b_nk ? "_nk" : "_kn");
+    impl = std::string("gemm_ffma_") + dtype_name(s.dtype) + (s.b_nk ? "_nk" : "_kn");
+    const int sms = ctx->sm_count;
     switch (s.dtype) {
-        case DType::F32: return ffma_launch<float, float>(s, false);
-        case DType::TF32: return ffma_launch<float, float>(s, true);
+        case DType::F32: return ffma_launch<float, float>(s, false, sms, impl);
+        case DType::TF32: return ffma_launch<float, float>(s, true, sms, impl);
         case DType::BF16:
-            return s.out_dtype == DType::BF16 ? ffma_launch<__nv_bfloat16, __nv_bfloat16>(s, false) : ffma_launch<__nv_bfloat16, float>(s, false);
+            return s.out_dtype == DType::BF16 ? ffma_launch<__nv_bfloat16, __nv_bfloat16>(s, false, sms, impl)
+                                              : ffma_launch<__nv_bfloat16, float>(s, false, sms, impl);
         case DType::F16:
-            return s.out_dtype == DType::F16 ? ffma_launch<__half, __half>(s, false) : ffma_launch<__half, float>(s, false);
+            return s.out_dtype == DType::F16 ? ffma_launch<__half, __half>(s, false, sms, impl)
+                                             : ffma_launch<__half, float>(s, false, sms, impl);
         default: throw IrError("unsupported GEMM dtype");
     }
 }

@@ -94,8 +94,35 @@ class ResidualMLP:
         (so folding it is the identity); generated on device directly in the packed
         layout, the shard's own stream of the counter-based generator."""
         self.rt.fill(self.x, "normal", seed=seed, stream=0, lo=0.0, hi=1.0)
-        self.rt.fill(self.wgu, "normal", seed=seed, stream=100 + self.rank, lo=0.0, hi=std)
-        self.rt.fill(self.wd, "normal", seed=seed, stream=200 + self.rank, lo=0.0, hi=std)
+        fill_synthetic_shard(self.rt, self.wgu, self.wd, self.rank, seed, std)
+
+
+def fill_synthetic_shard(rt: Runtime, wgu, wd, rank: int, seed: int = 0, std: float = 0.02) -> None:
+    """The packed gate/up weights [2f, d] and down weights [d, f] of shard `rank`
+    of the synthetic block (each shard has its own generator streams, so any
+    process can regenerate any shard)."""
+    rt.fill(wgu, "normal", seed=seed, stream=100 + rank, lo=0.0, hi=std)
+    rt.fill(wd, "normal", seed=seed, stream=200 + rank, lo=0.0, hi=std)
+
+
+def synthetic_weights(rt: Runtime, width: int, hidden: int, tp: int, seed: int = 0, std: float = 0.02):
+    """Every shard of the synthetic block's weights regenerated on `rt`'s device
+    and returned in the reference's layout as FP32 host arrays: wg, wu [d, ffn]
+    and wd [ffn, d] (the values the shards hold, BF16-rounded)."""
+    f = hidden // tp
+    wg_parts, wu_parts, wd_parts = [], [], []
+    wgu, wd = rt.alloc(2 * f * width, "bf16"), rt.alloc(width * f, "bf16")
+    try:
+        for r in range(tp):
+            fill_synthetic_shard(rt, wgu, wd, r, seed, std)
+            g, u = unpack_gate_up(rt.download_f32(wgu).reshape(2 * f, width), width)
+            wg_parts.append(g)
+            wu_parts.append(u)
+            wd_parts.append(rt.download_f32(wd).reshape(width, f).T)
+    finally:
+        wgu.free()
+        wd.free()
+    return np.concatenate(wg_parts, axis=1), np.concatenate(wu_parts, axis=1), np.concatenate(wd_parts, axis=0)
 
     def load(self, x, norm_weight, wg, wu, wd) -> None:
         """Host FP32 weights in the reference's layout: wg, wu [d, ffn], wd [ffn, d]."""
