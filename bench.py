@@ -47,6 +47,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GEMM & causal-attention TFLOP/s, MLP-block tokens/s at 1/2/4/8 B200"
+MLP_CHUNKS, MLP_SM_LIMIT = [4], [132]  # tensor-parallel MLP: row blocks, GEMM CTAs (set by --mlp-*)
 B, H, S, D = 4, 16, 2048, 128
 
 
@@ -314,19 +315,24 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     rank = dist.get_rank() if dist is not None else 0
     if world > 1:
         parallel.init_comm(rt, dist, timeout_ms=120000)
-    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank)
+    # tensor parallel: 4 row blocks, each block's all-reduce on the collective
+    # stream beside the next block's GEMMs, whose grids leave SMs for NCCL
+    chunks, sm_limit = (1, 0) if world == 1 else (MLP_CHUNKS[0], MLP_SM_LIMIT[0])
+    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit)
     mlp.fill_synthetic(seed=11)
     jobs = mlp.jobs()
-    rt.execute(jobs, repeats=max(warmup, 3))
+    lanes = world > 1
+    rt.execute(jobs, repeats=max(warmup, 3), streams=lanes)
     barrier(dist)
     with ClockSampler(rt.device) as clk:
-        t = rt.execute(jobs, repeats=steps, per_job=True)
+        t = rt.execute(jobs, repeats=steps, per_job=True, streams=lanes)
     ms = reduce_max(dist, t.gpu_ms / steps)
     flops = 6.0 * T * d * ffn
     per_gpu_tflops = flops / world / (ms * 1e-3) / 1e12
     out = {"workload": f"residual MLP block T={T} d={d} ffn={ffn} BF16 (BASELINE configs[3]), tensor parallel x{world}",
            "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
            "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": [x / steps for x in t.job_ms],
+           "row_blocks": chunks, "gemm_sm_limit": sm_limit or None,
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
            "kernels": [k.info.get("impl") for k, _ in jobs], "clocks": clk.summary()}
@@ -468,10 +474,10 @@ def mlp_error(rt, mlp, world, seed, rows=(0, 1, 4097, 8191)):
     from jade_compute_b200.mlp import synthetic_weights
     rows = np.array(rows, np.int64)
     wg, wu, wd = synthetic_weights(rt, mlp.d, mlp.ffn, world, seed)
-    x = rt.download_f32(mlp.x)
+    x = mlp.download_x()
     ref, mag = O.mlp_rows_bf16h(mlp.d, mlp.ffn, x, np.ones(mlp.d, np.float32), wg, wu, wd, mlp.eps, rows,
                                 threads=host_threads())
-    got = np.stack([rt.download_f32(mlp.y, int(r) * mlp.d, mlp.d) for r in rows])
+    got = mlp.download_y_rows(rows)
     err = np.abs(got - ref)
     rms = float(np.sqrt((ref ** 2).mean()))
     return {"rows": len(rows), "max_err_over_m": float((err / mag).max()), "max_err_over_rms": float(err.max() / rms),
@@ -642,9 +648,13 @@ def _main(out_fd):
     ap.add_argument("--quick", action="store_true", help="headline only, no components")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--mlp-chunks", type=int, default=MLP_CHUNKS[0], help="row blocks of the tensor-parallel MLP")
+    ap.add_argument("--mlp-sm-limit", type=int, default=MLP_SM_LIMIT[0],
+                    help="persistent CTAs of the tensor-parallel MLP's GEMMs (0 = one per SM)")
     ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "ffma", "mlp", "rows", "sweep"], default=None,
                     help="run one workload alone (profiling), printing its own measurement")
     args = ap.parse_args()
+    MLP_CHUNKS[0], MLP_SM_LIMIT[0] = args.mlp_chunks, args.mlp_sm_limit
     if args.warmup < 3:
         args.warmup = 3
     return run_reference(args) if args.impl == "reference" else run_ours(args)

@@ -111,7 +111,9 @@ typedef struct jr_dispatch {
 #define JR_EXEC_GRAPH 1u /* capture one pass as a CUDA graph, replay it `repeats` times */
 /* Dependency-scheduled streams (not with JR_EXEC_GRAPH): host-to-device copy jobs
  * run on a transfer-in stream, device-to-host copy jobs on a transfer-out stream,
- * every other job on the context stream; each job first waits for the jobs it
+ * all_reduce jobs on a collective stream (so that the all-reduce of one row block
+ * overlaps the kernels of the next), every other job on the context stream;
+ * each job first waits for the jobs it
  * conflicts with on its bindings (read after write, write after write, write after
  * read), so results equal in-order execution while transfers overlap compute and
  * each other (e.g. one repeat's result read-back with the next repeat's uploads).

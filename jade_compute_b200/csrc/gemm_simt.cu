@@ -12,6 +12,9 @@
 // least one tile per SM, else 32x64 tiles of 4x4 per thread (128 threads), which
 // spread a small GEMM (512^3: 128 blocks instead of 16) over the SMs; the k
 // order of every sum is the same in both.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "internal.hpp"
 
@@ -161,11 +164,174 @@ LaunchFn ffma_launch_tiles(const Spec &s, bool tf32) {
     };
 }
 
-// 128x128 tiles when there is at least one per SM, else 32x64 tiles.
+// ------------------------------------------------------------------ FP32, TMA-fed
+// FP32 A [M,K] . B [K,N] with both strides multiples of 16 bytes: the operand
+// tiles arrive by TMA (cp.async.bulk.tensor) into a STAGES-deep shared-memory
+// ring, k tiles of 16, one mbarrier per stage, so that STAGES-1 tiles are in
+// flight while one is multiplied (the register-staged kernel above keeps one
+// 8-wide k tile in flight and measured latency-bound: 26 FFMA/clk/SM). A lands
+// row-major [BM][16]: a thread reads a float4 of 4 consecutive k per row it owns;
+// B lands [16][BN]. Each output still sums its k products in order with one fmaf
+// each (the ring only changes when operands arrive), so the result is the same
+// bits as the sequential FP32 sum. Out-of-range rows, columns and k are
+// zero-filled by TMA and never stored.
+constexpr int kTmaBK = 16;
+
+template <int BM, int BN, int TM, int TN, int STAGES>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    gemm_ffma_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float *__restrict__ C, int M,
+                         int N, int K, int *err) {
+    constexpr int kGroupsM = TM / 4, kGroupsN = TN / 4;
+    constexpr int kRowStride = BM / kGroupsM, kColStride = BN / kGroupsN;
+    constexpr uint32_t kStageA = BM * kTmaBK * 4, kStageB = kTmaBK * BN * 4;
+    extern __shared__ uint8_t smem_raw[];
+    float *ring = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    __shared__ uint64_t full[STAGES];
+    __shared__ int abort_flag;
+    const int t = threadIdx.x;
+    const int tx = t % (BN / TN), ty = t / (BN / TN);
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int ktiles = (K + kTmaBK - 1) / kTmaBK;
+    auto stage_a = [&](int s) { return ring + s * ((kStageA + kStageB) / 4); };
+    auto stage_b = [&](int s) { return ring + s * ((kStageA + kStageB) / 4) + kStageA / 4; };
+    auto issue = [&](int kt) {
+        const int s = kt % STAGES;
+        mbar_arrive_expect_tx(&full[s], kStageA + kStageB);
+        tma_load_2d(stage_a(s), &tmA, &full[s], kt * kTmaBK, m0);
+        tma_load_2d(stage_b(s), &tmB, &full[s], n0, kt * kTmaBK);
+    };
+    if (t == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+        abort_flag = 0;
+        fence_barrier_init();
+        fence_proxy_async();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        for (int kt = 0; kt < STAGES - 1 && kt < ktiles; ++kt) issue(kt);
+    }
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+    int issued = min(STAGES - 1, ktiles);
+    bool failed = false;
+    for (int kt = 0; kt < ktiles; ++kt) {
+        // every thread is done with tile kt-1, so its slot takes tile kt+STAGES-1;
+        // the vote also ends the loop in every thread at once after an expired wait
+        if (__syncthreads_or(failed)) break;
+        if (t == 0 && issued < ktiles) issue(issued);
+        ++issued;
+        const int s = kt % STAGES;
+        if (!mbar_wait(&full[s], (kt / STAGES) & 1, &abort_flag, err, kErrWaitTmaFull)) {
+            failed = true;
+            continue;
+        }
+        const float *as = stage_a(s), *bs = stage_b(s);
+#pragma unroll
+        for (int k4 = 0; k4 < kTmaBK; k4 += 4) {
+            float a[TM][4], b[4][TN];
+#pragma unroll
+            for (int i = 0; i < TM; ++i) {
+                const int r = (i / 4) * kRowStride + ty * 4 + (i % 4);
+                const float4 v = *reinterpret_cast<const float4 *>(as + r * kTmaBK + k4);
+                a[i][0] = v.x; a[i][1] = v.y; a[i][2] = v.z; a[i][3] = v.w;
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int g = 0; g < kGroupsN; ++g) {
+                    const float4 v = *reinterpret_cast<const float4 *>(bs + (k4 + q) * BN + g * kColStride + tx * 4);
+                    b[q][4 * g] = v.x; b[q][4 * g + 1] = v.y; b[q][4 * g + 2] = v.z; b[q][4 * g + 3] = v.w;
+                }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int i = 0; i < TM; ++i)
+#pragma unroll
+                    for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i][q], b[q][j], acc[i][j]);
+        }
+    }
+    if (__syncthreads_or(failed)) {
+        // the last copy issued into each slot lands before the CTA's shared memory
+        // is released (a copy that never lands ends the drain at the time limit)
+        if (t == 0) {
+            const int n_issued = min(issued, ktiles);
+            for (int kt = max(0, n_issued - STAGES); kt < n_issued; ++kt) mbar_wait_drain(&full[kt % STAGES], (kt / STAGES) & 1, err);
+        }
+        return;
+    }
+    const bool vec = (N % 4) == 0;
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int r = m0 + (i / 4) * kRowStride + ty * 4 + (i % 4);
+        if (r >= M) continue;
+#pragma unroll
+        for (int g = 0; g < kGroupsN; ++g) {
+            const int c = n0 + g * kColStride + tx * 4;
+            float *dst = C + (size_t)r * N + c;
+            if (vec && c + 4 <= N) {
+                *reinterpret_cast<float4 *>(dst) = make_float4(acc[i][4 * g], acc[i][4 * g + 1], acc[i][4 * g + 2], acc[i][4 * g + 3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (c + e < N) dst[e] = acc[i][4 * g + e];
+            }
+        }
+    }
+}
+
+using TiledEncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *, const cuuint64_t *,
+                                   const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Row-major FP32 [rows, cols] described to TMA without swizzle, box {box_cols, box_rows}.
+bool fp32_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_cols, uint32_t box_rows) {
+    static const auto enc = reinterpret_cast<TiledEncodeFn>(driver_entry("cuTensorMapEncodeTiled"));
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BM, int BN, int TM, int TN, int STAGES>
+LaunchFn ffma_tma_launch(Context *ctx, const Spec &s) {
+    auto kernel = gemm_ffma_tma_kernel<BM, BN, TM, TN, STAGES>;
+    constexpr int threads = (BM / TM) * (BN / TN);
+    constexpr int smem = STAGES * (BM + BN) * kTmaBK * 4 + 128;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        throw IrError("cannot reserve shared memory for the FFMA GEMM");
+    const int M = (int)s.m, N = (int)s.n, K = (int)s.k;
+    const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    int *err = ctx->err_dev;
+    return [=](cudaStream_t st, void **b) {
+        CUtensorMap ma, mb;
+        if (!fp32_map(&ma, b[0], M, K, kTmaBK, BM) || !fp32_map(&mb, b[1], K, N, BN, kTmaBK)) return cudaErrorInvalidValue;
+        kernel<<<grid, threads, smem, st>>>(ma, mb, static_cast<float *>(b[2]), M, N, K, err);
+        return cudaGetLastError();
+    };
+}
+
+// FP32 (no epilogue, B [K,N]) with 16-byte strides takes the TMA-fed kernel.
+bool ffma_tma_fits(const Spec &s) {
+    return s.dtype == DType::F32 && !s.b_nk && !s.row_scale && s.epilogue == "none" && s.k % 4 == 0 && s.n % 4 == 0;
+}
+
+// 128x128 tiles when there is at least one per SM, else 32x64 tiles;
+// JADE_FFMA_TILE=128x128 or 32x64 forces one (read when a kernel is compiled).
 template <typename TA, typename TO>
 LaunchFn ffma_launch(const Spec &s, bool tf32, int sm_count, std::string &impl) {
     const long long big_tiles = (long long)((s.m + 127) / 128) * ((s.n + 127) / 128);
-    if (big_tiles >= sm_count) {
+    bool big = big_tiles >= sm_count;
+    if (const char *force = std::getenv("JADE_FFMA_TILE"); force && *force) {
+        if (!std::strcmp(force, "128x128")) big = true;
+        else if (!std::strcmp(force, "32x64")) big = false;
+        else throw IrError("JADE_FFMA_TILE must be 128x128 or 32x64");
+    }
+    if (big) {
         impl += "_128x128";
         return ffma_launch_tiles<TA, TO, 128, 128, 8, 8>(s, tf32);
     }
@@ -179,6 +345,16 @@ LaunchFn make_gemm_simt(Context *ctx, const Spec &s, std::string &impl) {
     if (s.epilogue == "swiglu") throw IrError("swiglu epilogue needs the tcgen05 path (K a multiple of 8)");
     impl = std::string("gemm_ffma_") + dtype_name(s.dtype) + (s.b_nk ? "_nk" : "_kn");
     const int sms = ctx->sm_count;
+    const char *force = std::getenv("JADE_FFMA_TILE");
+    if (ffma_tma_fits(s) && !(force && *force)) {
+        const long long big_tiles = (long long)((s.m + 127) / 128) * ((s.n + 127) / 128);
+        if (big_tiles >= sms) {
+            impl += "_tma_128x128";
+            return ffma_tma_launch<128, 128, 8, 8, 4>(ctx, s);
+        }
+        impl += "_tma_32x64";
+        return ffma_tma_launch<32, 64, 4, 4, 4>(ctx, s);
+    }
     switch (s.dtype) {
         case DType::F32: return ffma_launch<float, float>(s, false, sms, impl);
         case DType::TF32: return ffma_launch<float, float>(s, true, sms, impl);

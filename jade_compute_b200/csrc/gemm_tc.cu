@@ -120,6 +120,60 @@ __device__ __forceinline__ void store32<__half>(__half *dst, const float (&v)[32
     store32_16(dst, v, valid, vec_ok);
 }
 
+// One epilogue lane's share of a 32-column chunk of the residual: rows
+// row0 + 4 i + r_sub (i = 0..7), four consecutive columns each, kept as raw words
+// (two 16-bit values or one FP32 value per word) until they are added, so the
+// loads of a chunk are all in flight while the previous chunk is stored.
+template <typename TOut>
+struct ResidualChunk {
+    static constexpr int kWords = sizeof(TOut);  // 4 values of TOut
+    uint32_t w[8][kWords];
+};
+
+template <typename TOut>
+__device__ __forceinline__ void load_residual(ResidualChunk<TOut> &r, const TOut *__restrict__ res, int row0, int r_sub, int gcol, int M,
+                                              int N, bool vec_ok) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int grow = row0 + 4 * i + r_sub;
+#pragma unroll
+        for (int q = 0; q < ResidualChunk<TOut>::kWords; ++q) r.w[i][q] = 0;
+        if (grow >= M || gcol >= N) continue;
+        const TOut *p = res + (size_t)grow * N + gcol;
+        if (vec_ok && gcol + 4 <= N) {
+            if constexpr (sizeof(TOut) == 4) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
+                r.w[i][0] = v.x; r.w[i][1] = v.y; r.w[i][2] = v.z; r.w[i][3] = v.w;
+            } else {
+                const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+                r.w[i][0] = v.x; r.w[i][1] = v.y;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (gcol + e >= N) break;
+                if constexpr (sizeof(TOut) == 4) {
+                    r.w[i][e] = __ldg(reinterpret_cast<const uint32_t *>(p) + e);
+                } else {
+                    const uint32_t h = __ldg(reinterpret_cast<const unsigned short *>(p) + e);
+                    r.w[i][e >> 1] |= h << ((e & 1) * 16);
+                }
+            }
+        }
+    }
+}
+
+template <typename TOut>
+__device__ __forceinline__ float residual_value(const ResidualChunk<TOut> &r, int i, int e) {
+    if constexpr (sizeof(TOut) == 4) {
+        return __uint_as_float(r.w[i][e]);
+    } else {
+        const uint32_t h = (r.w[i][e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+        if constexpr (std::is_same<TOut, __nv_bfloat16>::value) return __uint_as_float(h << 16);
+        else return __half2float(__ushort_as_half((unsigned short)h));
+    }
+}
+
 template <int kEB, uint32_t kFmt, bool kBmn, typename TOut, int kEpi, bool kRowScale>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
@@ -235,9 +289,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_in_tile = quarter * 32 + lane;
         int acc = 0;
         uint32_t acc_phase = 0;
+        const int r_sub = lane >> 3, c_sub = (lane & 7) * 4;  // this lane's row in each group of 4, its columns
+        ResidualChunk<TOut> res_next;
         for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
             int tm, tn;
             tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+            if constexpr (kEpi == kEpiResidual)  // the residual does not wait for the MMAs: fetch chunk 0 now
+                load_residual(res_next, static_cast<const TOut *>(args.residual), tm * BM + quarter * 32, r_sub, tn * BN + c_sub,
+                              args.M, args.N, (args.N % 4) == 0);
             if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, err, kErrWaitAccFull)) break;
             tc_fence_after();
             const int row = tm * BM + row_in_tile;
@@ -270,12 +329,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // of a 128 x 256 FP32 tile take ~5 us.
                 float *blk = reinterpret_cast<float *>(smem + kStages * kStageBytes + 256) + (warp - 2) * (32 * 33);
                 const int c0 = tn * BN, row0 = tm * BM + quarter * 32;
-                const int r_sub = lane >> 3, c_sub = (lane & 7) * 4;  // this lane's row in each group of 4, its columns
                 const bool vec_ok = (args.N % 4) == 0;
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 32) {
                     const int col = c0 + c;
                     if (col >= args.N) break;  // uniform across the warp
+                    ResidualChunk<TOut> res_cur;
+                    if constexpr (kEpi == kEpiResidual) {
+                        res_cur = res_next;
+                        if (c + 32 < BN)  // next chunk's residual in flight during this chunk's stores
+                            load_residual(res_next, static_cast<const TOut *>(args.residual), row0, r_sub, col + 32 + c_sub, args.M, args.N,
+                                          vec_ok);
+                    }
                     uint32_t r[32];
                     tmem_ld32(tbase + c, r);
                     tmem_wait_ld();
@@ -290,10 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int e = 0; e < 4; ++e) v[e] = blk[rl * 33 + c_sub + e];
                             if constexpr (kEpi == kEpiResidual) {
-                                const TOut *res = static_cast<const TOut *>(args.residual) + (size_t)grow * args.N + gcol;
 #pragma unroll
-                                for (int e = 0; e < 4; ++e)
-                                    if (gcol + e < args.N) v[e] += to_f32(res[e]);
+                                for (int e = 0; e < 4; ++e) v[e] += residual_value(res_cur, i, e);
                             }
                             store4<TOut>(out + (size_t)grow * args.N + gcol, v, args.N - gcol, vec_ok);
                         }
@@ -357,7 +420,7 @@ LaunchFn tc_launch(Context *ctx, const Spec &s) {
     base.num_tiles = base.tiles_m * base.tiles_n;
     base.kblocks = (int)((s.k + (128 / kEB) - 1) / (128 / kEB));
     base.err = ctx->err_dev;
-    const int grid = std::min(base.num_tiles, ctx->sm_count);
+    const int grid = std::min(base.num_tiles, s.sm_limit ? std::min<int>((int)s.sm_limit, ctx->sm_count) : ctx->sm_count);
     const uint64_t M = s.m, K = s.k;
     return [=](cudaStream_t st, void **b) {
         CUtensorMap ma, mb;

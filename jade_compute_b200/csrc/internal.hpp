@@ -30,8 +30,9 @@ struct Context {
     int *err_host = nullptr;  // mapped, written by kernels (first error wins)
     int *err_dev = nullptr;
     std::vector<cudaEvent_t> job_events;
-    // JR_EXEC_STREAMS: transfer streams (created on first use) and dependency events
-    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    // JR_EXEC_STREAMS: transfer and collective streams (created on first use) and
+    // dependency events
+    cudaStream_t copy_in = nullptr, copy_out = nullptr, collective = nullptr;
     std::vector<cudaEvent_t> dep_events;
     // NCCL (opaque; see comm.cpp)
     void *nccl_comm = nullptr;

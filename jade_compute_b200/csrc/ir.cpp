@@ -145,7 +145,7 @@ DType parse_dtype(const std::string &s) {
 }
 
 bool Spec::extended() const {
-    return has_dtype || has_out_dtype || has_batch || has_b_layout || epilogue != "none" || row_scale ||
+    return has_dtype || has_out_dtype || has_batch || has_b_layout || epilogue != "none" || row_scale || sm_limit ||
            op == Op::RmsInv || op == Op::AllReduce || op == Op::Copy || op == Op::L2Flush || op == Op::Fill;
 }
 
@@ -212,6 +212,7 @@ Spec parse_spec(const Json &j) {
         if (j.has("stream")) s.stream_id = get_u32(j, "stream");
         if (j.has("lo")) s.lo = get_f32(j, "lo");
         if (j.has("hi")) s.hi = get_f32(j, "hi");
+        if (j.has("offset")) s.offset = get_uint(j, "offset", UINT64_MAX);
     } else {
         bail("unknown variant `" + op + "`, expected one of `elementwise`, `axpy`, `add`, `gemm`, `gemm_simd`, `gemm_mps`, "
              "`attention_scores`, `attention_apply`, `attention_online`, `rms_norm`, `swi_glu`, `softmax`, "
@@ -240,6 +241,7 @@ Spec parse_spec(const Json &j) {
         s.epilogue = d->text;
     }
     if (j.has("row_scale")) s.row_scale = get_bool(j, "row_scale");
+    if (j.has("sm_limit")) s.sm_limit = get_u32(j, "sm_limit");
     return s;
 }
 
@@ -278,6 +280,7 @@ Json spec_to_json(const Spec &s) {
         case Op::Fill:
             j.set("op", Json::str("fill")).set("len", U(s.len)).set("dist", Json::str(s.dist)).set("seed", U(s.seed))
                 .set("stream", U(s.stream_id)).set("lo", Json::f32(s.lo)).set("hi", Json::f32(s.hi));
+            if (s.offset) j.set("offset", U(s.offset));
             break;
     }
     if (s.has_dtype) j.set("dtype", Json::str(dtype_name(s.dtype)));
@@ -286,6 +289,7 @@ Json spec_to_json(const Spec &s) {
     if (s.has_b_layout) j.set("b_layout", Json::str(s.b_nk ? "nk" : "kn"));
     if (s.epilogue != "none") j.set("epilogue", Json::str(s.epilogue));
     if (s.row_scale) j.set("row_scale", Json::boolean(true));
+    if (s.sm_limit) j.set("sm_limit", U(s.sm_limit));
     return j;
 }
 
@@ -314,8 +318,8 @@ void validate(const Spec &s) {  // ir.rs:193-268 plus the extensions
             else check_dtype(s, {DType::F32});
             ensure(s.out_dtype == DType::F32 || (is16(s.dtype) && s.out_dtype == s.dtype),
                    "gemm out_dtype must be fp32 or the 16-bit input type");
-            if (s.epilogue != "none" || s.row_scale || s.b_nk)
-                ensure(s.dtype != DType::F32, "GEMM fusion and b_layout nk need a tensor-core dtype (tf32, bf16, fp16)");
+            if (s.epilogue != "none" || s.row_scale || s.b_nk || s.sm_limit)
+                ensure(s.dtype != DType::F32, "GEMM fusion, b_layout nk and sm_limit need a tensor-core dtype (tf32, bf16, fp16)");
             ensure(s.epilogue == "none" || s.epilogue == "swiglu" || s.epilogue == "residual",
                    "epilogue must be none, swiglu or residual");
             if (s.epilogue == "swiglu") {

@@ -70,6 +70,8 @@ struct Spec {
     uint64_t seed = 0;
     uint32_t stream_id = 0;
     float lo = 0, hi = 1;
+    uint64_t offset = 0;    // fill: generator index of element 0 (a slice of a larger fill)
+    uint32_t sm_limit = 0;  // tcgen05 gemm: at most this many persistent CTAs (0 = one per SM)
     bool extended() const;
 };
 

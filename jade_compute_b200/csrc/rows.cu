@@ -456,14 +456,16 @@ __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 // Counter-based synthetic inputs: element i of stream s from seed is
-// splitmix64(seed ^ s*C ^ i); uniform in [lo, hi) or normal (Box-Muller) with
+// splitmix64(seed ^ s*C ^ (offset + i)) (offset: this buffer is a slice of a
+// larger generated tensor); uniform in [lo, hi) or normal (Box-Muller) with
 // mean lo and standard deviation hi; rounded once to the output type.
 template <typename T>
-__global__ void fill_kernel(T *__restrict__ out, uint64_t n, uint64_t seed, uint32_t stream, int normal, float lo, float hi) {
+__global__ void fill_kernel(T *__restrict__ out, uint64_t n, uint64_t seed, uint32_t stream, int normal, float lo, float hi,
+                            uint64_t offset) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t key = splitmix64(seed ^ (0xD1B54A32D192ED03ull * (uint64_t)(stream + 1)));
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint64_t h = splitmix64(key + i);
+        const uint64_t h = splitmix64(key + offset + i);
         float v;
         if (normal) {
             const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);            // (0,1)
@@ -533,7 +535,7 @@ LaunchFn make_row_kernel(Context *ctx, const Spec &s, std::string &impl) {
 
 LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl) {
     if (s.op == Op::Fill) {
-        const uint64_t n = s.len, seed = s.seed;
+        const uint64_t n = s.len, seed = s.seed, offset = s.offset;
         const uint32_t stream = s.stream_id;
         const int normal = s.dist == "normal";
         const float lo = s.lo, hi = s.hi;
@@ -541,9 +543,9 @@ LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl) {
         impl = std::string("fill_") + s.dist + "_" + dtype_name(s.dtype);
         const DType d = s.dtype;
         return [=](cudaStream_t st, void **b) {
-            if (d == DType::BF16) fill_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>((__nv_bfloat16 *)b[0], n, seed, stream, normal, lo, hi);
-            else if (d == DType::F16) fill_kernel<__half><<<grid, kThreads, 0, st>>>((__half *)b[0], n, seed, stream, normal, lo, hi);
-            else fill_kernel<float><<<grid, kThreads, 0, st>>>((float *)b[0], n, seed, stream, normal, lo, hi);
+            if (d == DType::BF16) fill_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>((__nv_bfloat16 *)b[0], n, seed, stream, normal, lo, hi, offset);
+            else if (d == DType::F16) fill_kernel<__half><<<grid, kThreads, 0, st>>>((__half *)b[0], n, seed, stream, normal, lo, hi, offset);
+            else fill_kernel<float><<<grid, kThreads, 0, st>>>((float *)b[0], n, seed, stream, normal, lo, hi, offset);
             return cudaGetLastError();
         };
     }

@@ -76,7 +76,7 @@ void teardown(Context *ctx) {
     for (cudaEvent_t e : ctx->dep_events) cudaEventDestroy(e);
     for (cudaEvent_t e : {ctx->start, ctx->stop})
         if (e) cudaEventDestroy(e);
-    for (cudaStream_t s : {ctx->copy_in, ctx->copy_out, ctx->stream})
+    for (cudaStream_t s : {ctx->copy_in, ctx->copy_out, ctx->collective, ctx->stream})
         if (s) cudaStreamDestroy(s);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     delete ctx;
@@ -528,7 +528,9 @@ struct CapturedPass {
 };
 
 // JR_EXEC_STREAMS placement: lane 0 is the context stream, lane 1 takes
-// host-to-device copies and lane 2 device-to-host copies. Every launch records
+// host-to-device copies, lane 2 device-to-host copies and lane 3 collectives
+// (so that an all-reduce of one block overlaps the kernels of the next, which
+// do not touch its buffer). Every launch records
 // an event; before a launch, its lane waits for the latest conflicting launch on
 // each other lane (a write to a buffer it touches; for an output, also reads of
 // it since that write). Launches within a lane are already ordered, so the
@@ -539,6 +541,7 @@ class LaneScheduler {
         lane_stream_[0] = ctx.stream;
         lane_stream_[1] = ctx.copy_in;
         lane_stream_[2] = ctx.copy_out;
+        lane_stream_[3] = ctx.collective;
         for (auto &row : waited_) std::fill(std::begin(row), std::end(row), -1L);
         lane_of_.reserve(launches);
         for (int l = 1; l < kLanes; ++l) check_cuda(cudaStreamWaitEvent(lane_stream_[l], ctx.start, 0), "kernel launch");
@@ -550,7 +553,8 @@ class LaneScheduler {
         const jade::Spec &sp = job.kernel->spec;
         int lane = 0;
         if (sp.op == jade::Op::Copy) lane = sp.direction == "h2d" ? 1 : sp.direction == "d2h" ? 2 : 0;
-        long hazard[kLanes] = {-1, -1, -1};
+        if (job.kernel->collective) lane = 3;
+        long hazard[kLanes] = {-1, -1, -1, -1};
         const auto &binds = job.kernel->binds;
         for (size_t b = 0; b < binds.size(); ++b) {
             const Uses &u = uses_[job.buffers[b]];
@@ -572,7 +576,7 @@ class LaneScheduler {
         last_[lane] = id;
         for (size_t b = 0; b < binds.size(); ++b) {
             Uses &u = uses_[job.buffers[b]];
-            if (binds[b].write) u = Uses{id, {-1, -1, -1}};
+            if (binds[b].write) u = Uses{id, {-1, -1, -1, -1}};
             else u.reader[lane] = id;
         }
     }
@@ -588,17 +592,17 @@ class LaneScheduler {
     }
 
   private:
-    static constexpr int kLanes = 3;
+    static constexpr int kLanes = 4;
     struct Uses {
         long writer = -1;
-        long reader[kLanes] = {-1, -1, -1};
+        long reader[kLanes] = {-1, -1, -1, -1};
     };
     Context &ctx_;
     cudaStream_t lane_stream_[kLanes];
     std::map<const void *, Uses> uses_;
     std::vector<int> lane_of_;
     long waited_[kLanes][kLanes];
-    long last_[kLanes] = {-1, -1, -1};
+    long last_[kLanes] = {-1, -1, -1, -1};
 };
 
 }  // namespace
@@ -626,7 +630,7 @@ extern "C" int jr_execute2(void *handle, const jr_dispatch *jobs, size_t job_cou
         if (lanes) {
             if (launches > 65536) raise(JR_EINVAL, "dependency-scheduled streams support at most 65536 job launches per call");
             const char *what = "create transfer streams/dependency events";
-            for (cudaStream_t *s : {&ctx.copy_in, &ctx.copy_out})
+            for (cudaStream_t *s : {&ctx.copy_in, &ctx.copy_out, &ctx.collective})
                 if (!*s) check_cuda(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking), what);
             reserve_events(ctx.dep_events, launches, cudaEventDisableTiming, what);
         }

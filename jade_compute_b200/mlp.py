@@ -15,6 +15,9 @@ as four ordered jobs instead of six dispatches:
 Tensor parallelism over `tp` ranks splits ffn: rank r holds the gate/up columns
 and down-projection rows [r*ffn/tp, (r+1)*ffn/tp); the partial outputs are summed
 by one all-reduce after the down projection, the residual is added once (rank 0).
+With the tokens in row blocks, each block's all-reduce runs on the collective
+stream while the next block's GEMMs run (the batch's dependency scheduling
+orders them by the buffers they touch).
 """
 from __future__ import annotations
 
@@ -53,49 +56,99 @@ def unpack_gate_up(packed: np.ndarray, d: int):
 
 
 class ResidualMLP:
-    """One tensor-parallel shard of the fused residual MLP, resident on one device."""
+    """One tensor-parallel shard of the fused residual MLP, resident on one device.
+
+    ``chunks`` splits the tokens into equal row blocks, each with its own x, inv,
+    h and y buffers and its own four jobs; run with ``streams=True`` the
+    all-reduce of block c (on the collective stream) overlaps the GEMMs of block
+    c+1. ``sm_limit`` caps the persistent CTAs of both GEMMs so that the
+    collective's kernels find free SMs beside them."""
 
     def __init__(self, rt: Runtime, tokens: int, width: int, hidden: int, tp: int = 1, rank: int = 0,
-                 eps: float = 1e-5, collective: bool = True):
+                 eps: float = 1e-5, collective: bool = True, chunks: int = 1, sm_limit: int = 0):
         self.rt, self.T, self.d, self.ffn, self.tp, self.rank, self.eps = rt, tokens, width, hidden, tp, rank, eps
         self.f = hidden // tp
         shard_columns(hidden, tp, rank)
-        T, d, f = tokens, width, self.f
-        self.x = rt.alloc(T * d, "bf16")
+        if chunks < 1 or tokens % chunks:
+            raise ValueError(f"tokens={tokens} must split into {chunks} equal row blocks")
+        self.chunks, self.Tc = chunks, tokens // chunks
+        Tc, d, f = self.Tc, width, self.f
+        self.xs = [rt.alloc(Tc * d, "bf16") for _ in range(chunks)]
+        self.invs = [rt.alloc(Tc, "fp32") for _ in range(chunks)]
+        self.hs = [rt.alloc(Tc * f, "bf16") for _ in range(chunks)]
+        self.ys = [rt.alloc(Tc * d, "bf16") for _ in range(chunks)]
         self.wgu = rt.alloc(2 * f * d, "bf16")
         self.wd = rt.alloc(d * f, "bf16")
-        self.inv = rt.alloc(T, "fp32")
-        self.h = rt.alloc(T * f, "bf16")
-        self.y = rt.alloc(T * d, "bf16")
         base = {"tiled": True, "dtype": "bf16", "b_layout": "nk", "out_dtype": "bf16"}
-        self.k_inv = rt.compile({"op": "rms_inv", "rows": T, "cols": d, "epsilon": eps, "dtype": "bf16"})
-        self.k_up = rt.compile({"op": "gemm", "m": T, "n": f, "k": d, "epilogue": "swiglu", "row_scale": True, **base})
-        down = {"op": "gemm", "m": T, "n": d, "k": f, **base}
+        if sm_limit:
+            base["sm_limit"] = sm_limit
+        self.k_inv = rt.compile({"op": "rms_inv", "rows": Tc, "cols": d, "epsilon": eps, "dtype": "bf16"})
+        self.k_up = rt.compile({"op": "gemm", "m": Tc, "n": f, "k": d, "epilogue": "swiglu", "row_scale": True, **base})
+        down = {"op": "gemm", "m": Tc, "n": d, "k": f, **base}
         if rank == 0:
             down["epilogue"] = "residual"
         self.k_down = rt.compile(down)
-        self.k_ar = rt.compile({"op": "all_reduce", "len": T * d, "dtype": "bf16"}) if tp > 1 and collective else None
+        self.k_ar = rt.compile({"op": "all_reduce", "len": Tc * d, "dtype": "bf16"}) if tp > 1 and collective else None
+
+    # single-block views (chunks == 1)
+    @property
+    def x(self):
+        if self.chunks != 1:
+            raise AttributeError("a chunked block keeps x in row blocks: use xs or download_x()")
+        return self.xs[0]
+
+    @property
+    def y(self):
+        if self.chunks != 1:
+            raise AttributeError("a chunked block keeps y in row blocks: use ys or download_y()")
+        return self.ys[0]
 
     def jobs(self):
-        j = [(self.k_inv, [self.x, self.inv]),
-             (self.k_up, [self.x, self.wgu, self.inv, self.h]),
-             (self.k_down, [self.h, self.wd, self.x, self.y] if self.rank == 0 else [self.h, self.wd, self.y])]
-        if self.k_ar is not None:
-            j.append((self.k_ar, [self.y]))
+        j = []
+        for x, inv, h, y in zip(self.xs, self.invs, self.hs, self.ys):
+            j += [(self.k_inv, [x, inv]),
+                  (self.k_up, [x, self.wgu, inv, h]),
+                  (self.k_down, [h, self.wd, x, y] if self.rank == 0 else [h, self.wd, y])]
+            if self.k_ar is not None:
+                j.append((self.k_ar, [y]))
         return j
 
     def flops(self) -> float:
         """Algorithmic FLOPs of this shard: 2*T*d*(2f) + 2*T*f*d."""
         return 6.0 * self.T * self.d * self.f
 
+    # -- host views
+    def download_x(self) -> np.ndarray:
+        return np.concatenate([self.rt.download_f32(b) for b in self.xs])
+
+    def download_y(self) -> np.ndarray:
+        return np.concatenate([self.rt.download_f32(b) for b in self.ys])
+
+    def download_y_rows(self, rows) -> np.ndarray:
+        """[len(rows), d] FP32 copies of the listed token rows of y."""
+        return np.stack([self.rt.download_f32(self.ys[int(r) // self.Tc], (int(r) % self.Tc) * self.d, self.d) for r in rows])
+
     # -- weights
     def fill_synthetic(self, seed: int = 0, std: float = 0.02) -> None:
         """BASELINE config 4 inputs: x ~ N(0,1), weights ~ N(0, std), norm weight 1
         (so folding it is the identity); generated on device directly in the packed
-        layout, the shard's own stream of the counter-based generator."""
-        self.rt.fill(self.x, "normal", seed=seed, stream=0, lo=0.0, hi=1.0)
+        layout, the shard's own stream of the counter-based generator. x is the same
+        tensor for any chunking (each block is a slice of one generated stream)."""
+        for c, x in enumerate(self.xs):
+            self.rt.fill(x, "normal", seed=seed, stream=0, lo=0.0, hi=1.0, offset=c * self.Tc * self.d)
         fill_synthetic_shard(self.rt, self.wgu, self.wd, self.rank, seed, std)
 
+    def load(self, x, norm_weight, wg, wu, wd) -> None:
+        """Host FP32 weights in the reference's layout: wg, wu [d, ffn], wd [ffn, d]."""
+        cols = shard_columns(self.ffn, self.tp, self.rank)
+        xb = f32_to_bf16(np.asarray(x, np.float32).ravel())
+        for c, buf in enumerate(self.xs):
+            self.rt.upload(buf, xb[c * self.Tc * self.d:(c + 1) * self.Tc * self.d])
+        wg = np.asarray(wg, np.float32).reshape(self.d, self.ffn)[:, cols]
+        wu = np.asarray(wu, np.float32).reshape(self.d, self.ffn)[:, cols]
+        self.rt.upload(self.wgu, f32_to_bf16(pack_gate_up(wg, wu, np.asarray(norm_weight, np.float32)).ravel()))
+        wd = np.asarray(wd, np.float32).reshape(self.ffn, self.d)[cols]
+        self.rt.upload(self.wd, f32_to_bf16(np.ascontiguousarray(wd.T).ravel()))  # [d, f] = nk layout
 
 def fill_synthetic_shard(rt: Runtime, wgu, wd, rank: int, seed: int = 0, std: float = 0.02) -> None:
     """The packed gate/up weights [2f, d] and down weights [d, f] of shard `rank`
@@ -123,13 +176,3 @@ def synthetic_weights(rt: Runtime, width: int, hidden: int, tp: int, seed: int =
         wgu.free()
         wd.free()
     return np.concatenate(wg_parts, axis=1), np.concatenate(wu_parts, axis=1), np.concatenate(wd_parts, axis=0)
-
-    def load(self, x, norm_weight, wg, wu, wd) -> None:
-        """Host FP32 weights in the reference's layout: wg, wu [d, ffn], wd [ffn, d]."""
-        cols = shard_columns(self.ffn, self.tp, self.rank)
-        self.rt.upload(self.x, f32_to_bf16(np.asarray(x, np.float32).ravel()))
-        wg = np.asarray(wg, np.float32).reshape(self.d, self.ffn)[:, cols]
-        wu = np.asarray(wu, np.float32).reshape(self.d, self.ffn)[:, cols]
-        self.rt.upload(self.wgu, f32_to_bf16(pack_gate_up(wg, wu, np.asarray(norm_weight, np.float32)).ravel()))
-        wd = np.asarray(wd, np.float32).reshape(self.ffn, self.d)[cols]
-        self.rt.upload(self.wd, f32_to_bf16(np.ascontiguousarray(wd.T).ravel()))  # [d, f] = nk layout

@@ -376,10 +376,15 @@ class Runtime:
                          list(jm) if per_job else None)
 
     # -- conveniences used by tests and benches
-    def fill(self, buf: Buffer, dist: str, seed: int, stream: int = 0, lo: float = 0.0, hi: float = 1.0) -> None:
-        """Counter-based synthetic input: uniform [lo, hi) or normal(mean=lo, std=hi)."""
+    def fill(self, buf: Buffer, dist: str, seed: int, stream: int = 0, lo: float = 0.0, hi: float = 1.0,
+             offset: int = 0) -> None:
+        """Counter-based synthetic input: uniform [lo, hi) or normal(mean=lo, std=hi).
+        ``offset``: the generator index of element 0, so that a buffer can hold a
+        slice [offset, offset + len) of a larger generated tensor."""
         spec = {"op": "fill", "len": buf.elements, "dist": dist, "seed": seed, "stream": stream, "lo": lo, "hi": hi,
                 "dtype": buf.dtype if buf.dtype != "tf32" else "fp32"}
+        if offset:
+            spec["offset"] = offset
         k = self.compile(spec)
         self.execute([(k, [buf])])
         k.release()

@@ -25,10 +25,12 @@ def main(out_dir):
     norm = rng.uniform(0.5, 1.5, d).astype(np.float32)
     wg, wu = ((rng.standard_normal((d, ffn)) * 0.05).astype(np.float32) for _ in range(2))
     wd = (rng.standard_normal((ffn, d)) * 0.05).astype(np.float32)
-    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank)
+    # two row blocks: block 0's all-reduce runs on the collective stream beside
+    # block 1's GEMMs
+    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=2, sm_limit=120)
     mlp.load(x, norm, wg, wu, wd)
-    rt.execute(mlp.jobs(), repeats=2)
-    np.save(os.path.join(out_dir, f"y_{rank}.npy"), rt.download_f32(mlp.y))
+    rt.execute(mlp.jobs(), repeats=2, streams=True)
+    np.save(os.path.join(out_dir, f"y_{rank}.npy"), mlp.download_y())
     dist.barrier()
     rt.comm_destroy()
     rt.close()

@@ -152,7 +152,9 @@ def test_mixed_chain_ordering(rt, gemm_op):
 
 
 GEMM_SHAPES = [(1, 1, 1), (7, 9, 13), (8, 8, 8), (31, 47, 19), (32, 32, 33), (33, 31, 65), (65, 67, 63),
-               (1, 129, 33), (64, 64, 64), (127, 65, 129), (256, 256, 65), (257, 263, 67)]
+               (1, 129, 33), (64, 64, 64), (127, 65, 129), (256, 256, 65), (257, 263, 67),
+               # K and N multiples of 4: the TMA-fed FFMA kernel (ragged M, N and k tiles)
+               (1, 4, 4), (33, 36, 20), (100, 68, 132), (129, 260, 516), (300, 128, 1024), (1100, 1200, 36)]
 
 
 @pytest.mark.parametrize("mnk", GEMM_SHAPES, ids=str)

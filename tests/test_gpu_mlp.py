@@ -76,7 +76,7 @@ def effective_oracle(rt, mlp_shards, rows):
     """FP64 chain on the weights the device actually holds (BF16, norm folded),
     h rounded to BF16; returns (reference rows, magnitude m)."""
     d = mlp_shards[0].d
-    x = rt.download_f32(mlp_shards[0].x)
+    x = mlp_shards[0].download_x()
     wg_parts, wu_parts, wd_parts = [], [], []
     for s in mlp_shards:
         wg, wu = unpack_gate_up(rt.download_f32(s.wgu).reshape(2 * s.f, d), d)
@@ -116,7 +116,7 @@ def test_fused_mlp_small_all_rows(rt, T, d, ffn):
     wd = (rng.standard_normal((ffn, d)) * 0.05).astype(np.float32)
     mlp.load(x, norm, wg, wu, wd)
     rt.execute(mlp.jobs(), repeats=2)
-    got = rt.download_f32(mlp.y).reshape(T, d)
+    got = mlp.download_y().reshape(T, d)
     rows = np.arange(T)
     check_mlp(got, effective_oracle(rt, [mlp], rows), ffn)
 
@@ -128,7 +128,7 @@ def test_fused_mlp_baseline_config4_sampled(rt):
     mlp.fill_synthetic(seed=3)
     rt.execute(mlp.jobs(), repeats=1)
     rows = np.array([0, 1, 4095, 8191, 127, 128, 5000, 6001])
-    got = rt.download_f32(mlp.y).reshape(T, d)[rows]
+    got = mlp.download_y_rows(rows)
     check_mlp(got, effective_oracle(rt, [mlp], rows), ffn)
 
 
@@ -145,9 +145,27 @@ def test_tensor_parallel_shards_sum_to_block(rt):
     for s in shards:
         s.load(x, norm, wg, wu, wd)
         rt.execute(s.jobs())
-        part = rt.download_f32(s.y).astype(np.float64)
+        part = s.download_y().astype(np.float64)
         total += part
         partial_size += np.abs(part)
     # each partial is rounded to BF16 once: 2^-8 |partial| per shard, no output rounding
     check_mlp(total.reshape(T, d), effective_oracle(rt, shards, np.arange(T)), ffn, out_rel=0.0,
               extra=(2.0 ** -8 * partial_size).reshape(T, d))
+
+
+def test_row_blocks_and_collective_lane_give_the_same_bits(rt):
+    # the block split into 4 row blocks with capped GEMM grids, run with the
+    # dependency-scheduled streams, equals the single block bit for bit (each
+    # output row's sums do not depend on the row tiling)
+    T, d, ffn = 1024, 512, 1024
+    whole = ResidualMLP(rt, T, d, ffn)
+    blocks = ResidualMLP(rt, T, d, ffn, chunks=4, sm_limit=100)
+    assert all("sm_limit" in k.spec for k in (blocks.k_up, blocks.k_down))
+    for m in (whole, blocks):
+        m.fill_synthetic(seed=5)
+    assert np.array_equal(whole.download_x(), blocks.download_x())
+    rt.execute(whole.jobs())
+    rt.execute(blocks.jobs(), repeats=2, streams=True)
+    assert np.array_equal(whole.download_y(), blocks.download_y())
+    rows = np.array([0, 255, 256, 1023])
+    assert np.array_equal(blocks.download_y_rows(rows), whole.download_y().reshape(T, d)[rows])

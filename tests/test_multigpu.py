@@ -38,7 +38,7 @@ def test_tensor_parallel_mlp_all_reduce_two_gpus(tmp_path):
         mlp = ResidualMLP(rt, T, d, ffn)
         mlp.load(x, norm, wg, wu, wd)
         rt.execute(mlp.jobs())
-        single = rt.download_f32(mlp.y).astype(np.float64)
+        single = mlp.download_y().astype(np.float64)
     finally:
         rt.close()
     scale = np.sqrt((single ** 2).mean())
