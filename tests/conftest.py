@@ -28,7 +28,9 @@ def _has_gpu() -> bool:
 
 
 HAS_GPU = _has_gpu()
-REF_ROOT = "/root/reference"
+# reference checkout (only this container's parity pins read it; GPU tests use the
+# prebuilt oracle/_ref): $JADE_REFERENCE_ROOT, else "reference" beside this repository
+REF_ROOT = os.environ.get("JADE_REFERENCE_ROOT") or os.path.join(os.path.dirname(ROOT), "reference")
 HAS_REF = os.path.isdir(REF_ROOT)
 
 

@@ -13,7 +13,8 @@ import json
 import os
 import sys
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = (sys.argv[1] if len(sys.argv) > 1 else os.environ.get("JADE_REFERENCE_ROOT")
+       or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference"))
 SRC = os.path.join(REF, "reports", "generated-native")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "emitter.json")
 
