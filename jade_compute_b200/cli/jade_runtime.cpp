@@ -752,6 +752,8 @@ int main(int argc, char **argv) {
                 write_file(dir + "/" + c.name + ".json", canon.c_str());
                 write_file(dir + "/" + c.name + ".metal", emit_text(compact, "metal"));
                 write_file(dir + "/" + c.name + ".cu", emit_text(compact, "corex"));
+                // this backend's sm_100a module of the case, beside the reference's CoreX text
+                write_file(dir + "/" + c.name + ".sm100a.cu", emit_text(compact, "cuda"));
                 // json! of the reference widens f32 fields to f64 (jade-runtime.rs:234)
                 std::function<void(Json &)> widen_f32 = [&](Json &j) {
                     if (j.kind == Json::Number && j.text.find_first_of(".eE") != std::string::npos) j = Json::f64((double)(float)j.num);
@@ -774,7 +776,7 @@ int main(int argc, char **argv) {
             Json m = Json::object();
             m.set("schema_version", Json::integer(1)).set("scope", Json::str("Generated source, not compilation or hardware validation")).set("cases", entries);
             write_file(dir + "/manifest.json", jade::to_string_pretty(m.sorted()));
-            printf("Generated Metal + CoreX kernels in %s\n", dir.c_str());
+            printf("Generated Metal + CoreX + CUDA sm_100a kernels in %s\n", dir.c_str());
             return 0;
         }
         if (backend == "metal") die("native Metal requires macOS");

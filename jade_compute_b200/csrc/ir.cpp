@@ -710,8 +710,6 @@ std::string cuda_elementwise_source(const Spec &s) {
     return o.str();
 }
 
-std::string cuda_source(const Spec &s) { return cuda_elementwise_source(s); }
-
 Json binding_to_json(const Binding &b) {
     Json j = Json::object();
     j.set("name", Json::str(b.name)).set("elements", Json::unsigned_(b.elements)).set("write", Json::boolean(b.write));
