@@ -28,6 +28,7 @@ enum DeviceError : int {
     kErrWaitPv = 7,         // attention correction waiting for PV
     kErrWaitDrain = 8,      // exit path waiting for copies in flight
     kErrBadLaunch = 9,      // launch geometry mismatch detected on device
+    kErrWaitProbe = 10,     // wait_probe: a wait that nothing satisfies, expired as designed
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -81,6 +82,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
         if (globaltimer() - t0 > JADE_WAIT_LIMIT_NS) {
+            if (err) atomicCAS(err, 0, code);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+// mbar_wait with a time limit given at run time (the wait_probe op).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err, int code,
+                                              uint64_t limit_ns) {
+    const uint64_t t0 = globaltimer();
+#pragma unroll 1
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > limit_ns) {
             if (err) atomicCAS(err, 0, code);
             *abort_flag = 1;
             return false;

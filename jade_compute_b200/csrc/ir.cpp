@@ -146,7 +146,7 @@ DType parse_dtype(const std::string &s) {
 
 bool Spec::extended() const {
     return has_dtype || has_out_dtype || has_batch || has_b_layout || epilogue != "none" || row_scale || sm_limit ||
-           op == Op::RmsInv || op == Op::AllReduce || op == Op::Copy || op == Op::L2Flush || op == Op::Fill;
+           op == Op::RmsInv || op == Op::AllReduce || op == Op::Copy || op == Op::L2Flush || op == Op::Fill || op == Op::WaitProbe;
 }
 
 const char *spec_name(const Spec &s) {
@@ -167,6 +167,7 @@ const char *spec_name(const Spec &s) {
         case Op::AllReduce: return "all_reduce";
         case Op::Copy: return "copy";
         case Op::L2Flush: return "l2_flush";
+        case Op::WaitProbe: return "wait_probe";
         case Op::Fill: return "fill";
     }
     return "?";
@@ -206,6 +207,7 @@ Spec parse_spec(const Json &j) {
     else if (op == "all_reduce") { s.op = Op::AllReduce; s.len = get_u32(j, "len"); }
     else if (op == "copy") { s.op = Op::Copy; s.bytes = get_uint(j, "bytes", UINT64_MAX); s.direction = get_str(j, "direction"); }
     else if (op == "l2_flush") { s.op = Op::L2Flush; s.bytes = get_uint(j, "bytes", UINT64_MAX); }
+    else if (op == "wait_probe") { s.op = Op::WaitProbe; s.limit_ns = get_uint(j, "limit_ns", UINT64_MAX); }
     else if (op == "fill") {
         s.op = Op::Fill; s.len = get_u32(j, "len"); s.dist = get_str(j, "dist");
         s.seed = get_uint(j, "seed", UINT64_MAX);
@@ -216,7 +218,7 @@ Spec parse_spec(const Json &j) {
     } else {
         bail("unknown variant `" + op + "`, expected one of `elementwise`, `axpy`, `add`, `gemm`, `gemm_simd`, `gemm_mps`, "
              "`attention_scores`, `attention_apply`, `attention_online`, `rms_norm`, `swi_glu`, `softmax`, "
-             "`rms_inv`, `all_reduce`, `copy`, `l2_flush`, `fill`");
+             "`rms_inv`, `all_reduce`, `copy`, `l2_flush`, `fill`, `wait_probe`");
     }
     if (const Json *d = j.get("dtype")) {
         if (d->kind != Json::String) bail("invalid type for `dtype`");
@@ -277,6 +279,7 @@ Json spec_to_json(const Spec &s) {
         case Op::AllReduce: j.set("op", Json::str("all_reduce")).set("len", U(s.len)); break;
         case Op::Copy: j.set("op", Json::str("copy")).set("bytes", U(s.bytes)).set("direction", Json::str(s.direction)); break;
         case Op::L2Flush: j.set("op", Json::str("l2_flush")).set("bytes", U(s.bytes)); break;
+        case Op::WaitProbe: j.set("op", Json::str("wait_probe")).set("limit_ns", U(s.limit_ns)); break;
         case Op::Fill:
             j.set("op", Json::str("fill")).set("len", U(s.len)).set("dist", Json::str(s.dist)).set("seed", U(s.seed))
                 .set("stream", U(s.stream_id)).set("lo", Json::f32(s.lo)).set("hi", Json::f32(s.hi));
@@ -361,6 +364,9 @@ void validate(const Spec &s) {  // ir.rs:193-268 plus the extensions
             ensure(s.direction == "h2d" || s.direction == "d2h" || s.direction == "d2d", "copy direction must be h2d, d2h or d2d");
             break;
         case Op::L2Flush: ensure(s.bytes >= (1u << 20), "l2_flush needs at least 1 MiB"); break;
+        case Op::WaitProbe:
+            ensure(s.limit_ns >= 1000 && s.limit_ns <= 10000000000ull, "wait_probe limit_ns must be 1e3..1e10");
+            break;
         case Op::Fill:
             dim(s.len);
             ensure(s.dist == "uniform" || s.dist == "normal", "fill dist must be uniform or normal");
@@ -428,6 +434,7 @@ std::vector<Binding> bindings(const Spec &s) {  // ir.rs:269-339
             break;
         }
         case Op::L2Flush: r = {b("scratch", s.bytes, true, DType::U8)}; break;
+        case Op::WaitProbe: r = {b("elapsed_ns", 2, true, DType::F32)}; break;
         case Op::Fill: r = {b("out", s.len, true, d)}; break;
     }
     return r;

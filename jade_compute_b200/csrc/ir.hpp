@@ -43,7 +43,7 @@ struct Expr {
 enum class Op {
     Elementwise, Axpy, Add, Gemm, GemmSimd, GemmMps, AttentionScores, AttentionApply,
     AttentionOnline, RmsNorm, SwiGlu, Softmax,
-    RmsInv, AllReduce, Copy, L2Flush, Fill
+    RmsInv, AllReduce, Copy, L2Flush, Fill, WaitProbe
 };
 
 struct Spec {
@@ -72,6 +72,7 @@ struct Spec {
     float lo = 0, hi = 1;
     uint64_t offset = 0;    // fill: generator index of element 0 (a slice of a larger fill)
     uint32_t sm_limit = 0;  // tcgen05 gemm: at most this many persistent CTAs (0 = one per SM)
+    uint64_t limit_ns = 0;  // wait_probe: the bounded wait's time limit
     bool extended() const;
 };
 

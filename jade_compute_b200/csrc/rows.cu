@@ -223,12 +223,15 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
             if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
                 for (int e = 0; e < N; ++e) m = fmaxf(m, v[j][e]);
+        // a thread whose elements are all -inf (masked scores) shifts by 0 instead of
+        // its own maximum, so that its exponentials are e^-inf = 0, not e^(-inf + inf)
+        const float shift = m == -INFINITY ? 0.0f : m;
         float s = 0.0f;
 #pragma unroll
         for (int j = 0; j < NV; ++j)
             if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
-                for (int e = 0; e < N; ++e) { v[j][e] = exp_neg(v[j][e] - m); s += v[j][e]; }
+                for (int e = 0; e < N; ++e) { v[j][e] = exp_neg(v[j][e] - shift); s += v[j][e]; }
         float mr = m, sr = s;
         block_reduce_softmax(mr, sr, scratch);
         const float inv = m == -INFINITY ? 0.0f : exp_neg(m - mr) / sr;  // a thread without elements stores nothing
@@ -479,6 +482,28 @@ __global__ void fill_kernel(T *__restrict__ out, uint64_t n, uint64_t seed, uint
     }
 }
 
+// Bounded-wait probe: thread 0 waits on an mbarrier that nothing arrives on,
+// through the same bounded wait as the tcgen05 kernels but with the spec's time
+// limit; on expiry it records kErrWaitProbe in the context's error word (which
+// the batch reports as JR_ETIMEOUT), stores how long it waited and returns. It
+// lets a test drive the expiry path on the GPU without a fault or a hang.
+__global__ void wait_probe_kernel(float *__restrict__ out, int *err, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = globaltimer();
+        const bool satisfied = mbar_wait_for(&bar, 0, &abort_flag, err, kErrWaitProbe, limit_ns);
+        out[0] = (float)(globaltimer() - t0);
+        out[1] = satisfied ? 1.0f : 0.0f;
+    }
+}
+
 __global__ void flush_kernel(uint4 *__restrict__ p, uint64_t n16, uint32_t salt) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride)
@@ -546,6 +571,15 @@ LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl) {
             if (d == DType::BF16) fill_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>((__nv_bfloat16 *)b[0], n, seed, stream, normal, lo, hi, offset);
             else if (d == DType::F16) fill_kernel<__half><<<grid, kThreads, 0, st>>>((__half *)b[0], n, seed, stream, normal, lo, hi, offset);
             else fill_kernel<float><<<grid, kThreads, 0, st>>>((float *)b[0], n, seed, stream, normal, lo, hi, offset);
+            return cudaGetLastError();
+        };
+    }
+    if (s.op == Op::WaitProbe) {
+        const uint64_t limit = s.limit_ns;
+        int *err = ctx->err_dev;
+        impl = "wait_probe";
+        return [=](cudaStream_t st, void **b) {
+            wait_probe_kernel<<<1, 32, 0, st>>>((float *)b[0], err, limit);
             return cudaGetLastError();
         };
     }

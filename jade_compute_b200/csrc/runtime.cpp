@@ -144,7 +144,8 @@ void raise_device_wait_error(Context &ctx) {
                                        "MMA wait for probabilities",
                                        "correction wait for P.V",
                                        "exit wait for copies in flight",
-                                       "launch geometry mismatch"};
+                                       "launch geometry mismatch",
+                                       "wait probe (a wait that nothing satisfies)"};
     const bool known = code > 0 && code < (int)(sizeof site / sizeof site[0]);
     raise(JR_ETIMEOUT, "device-side bounded wait expired: %s (code %d)", known ? site[code] : "unknown", code);
 }
@@ -408,7 +409,7 @@ void select_implementation(Context *ctx, jr_kernel &k) {
                 k.run = jade::make_attention_tc(ctx, s, k.impl);
             }
             return;
-        case Op::Fill: case Op::L2Flush:
+        case Op::Fill: case Op::L2Flush: case Op::WaitProbe:
             k.run = jade::make_misc_kernel(ctx, s, k.impl);
             k.path = "simt";
             return;

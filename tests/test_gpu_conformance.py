@@ -537,3 +537,26 @@ def test_abi1_emitted_cuda_modules(rt, emitted_modules, case):
     if spec["op"] in ("axpy", "add", "gemm", "swi_glu", "elementwise"):
         mine, _, _ = run(rt, spec, inputs)
         assert np.array_equal(mine, got), name
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("cols", [256, 1024, 8192])
+def test_softmax_rows_with_masked_scores(rt, dtype, cols):
+    # causal-masked score rows (as attention_scores writes them): row r keeps its
+    # first r+1 entries and holds -inf after them, so most threads of a row see
+    # only -inf and must contribute e^-inf = 0, not NaN
+    rows = 64
+    x = np.random.default_rng(cols).standard_normal((rows, cols)).astype(np.float32) * 4
+    keep = np.minimum(np.arange(rows) * (cols // rows) + 1, cols)
+    x[np.arange(cols)[None, :] >= keep[:, None]] = -np.inf
+    buf = rt.alloc(rows * cols, dtype)
+    rt.upload(buf, x.ravel() if dtype == "fp32" else jc.runtime.f32_to_bf16(x.ravel()))
+    out = rt.alloc(rows * cols, dtype)
+    k = rt.compile({"op": "softmax", "rows": rows, "cols": cols, "dtype": dtype})
+    rt.execute([(k, [buf, out])])
+    got = rt.download_f32(out)
+    assert np.isfinite(got).all()
+    exp = O.softmax(rows, cols, rt.download_f32(buf))
+    tol = (3e-5, 3e-5) if dtype == "fp32" else (2e-3, 2.0 ** -8)
+    rc, r = O.compare(got, exp, *tol)
+    assert rc == 0, (r.first_bad_index, r.max_abs_error)

@@ -200,3 +200,12 @@ def test_create_without_gpu_fails_cleanly():
     with pytest.raises(JadeError) as e:
         jc.Runtime(0)
     assert e.value.code in (1, 2)
+
+
+def test_wait_probe_spec():
+    spec = {"op": "wait_probe", "limit_ns": 1000000}
+    jc.spec_validate(spec)
+    assert [b["name"] for b in jc.spec_bindings(spec)] == ["elapsed_ns"]
+    rejects({"op": "wait_probe", "limit_ns": 10})
+    rejects({"op": "wait_probe", "limit_ns": 10**11})
+    rejects(spec, lambda s: jc.emit(s, "corex"))
