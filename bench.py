@@ -48,6 +48,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "GEMM & causal-attention TFLOP/s, MLP-block tokens/s at 1/2/4/8 B200"
 MLP_CHUNKS, MLP_SM_LIMIT = [0], [132]  # tensor-parallel MLP: row blocks (0 = by GPU count), GEMM CTAs
+MLP_COMM = ["nccl"]  # tensor-parallel MLP collective: nccl all-reduce or peer (NVLink scatter/reduce)
 B, H, S, D = 4, 16, 2048, 128
 
 
@@ -313,15 +314,23 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     from jade_compute_b200.mlp import ResidualMLP
     T, d, ffn = 8192, 4096, 14336
     rank = dist.get_rank() if dist is not None else 0
-    if world > 1:
+    if world > 1 and MLP_COMM[0] == "nccl":
         parallel.init_comm(rt, dist, timeout_ms=120000)
     # tensor parallel: row blocks, each block's all-reduce on the collective stream
     # beside the next block's GEMMs, whose grids leave SMs for NCCL. Smaller blocks
     # cost GEMM wave efficiency, so they pay only where the all-reduce is a large
     # share of the step (measured at 2 GPUs: one block is 9% faster than four)
-    chunks = MLP_CHUNKS[0] if MLP_CHUNKS[0] > 0 else {1: 1, 2: 1, 4: 2}.get(world, 4)
-    sm_limit = MLP_SM_LIMIT[0] if chunks > 1 else 0
-    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit)
+    comm = MLP_COMM[0] if world > 1 else "nccl"
+    if comm == "peer":
+        # the down GEMM scatters its partial rows to their owners over NVLink,
+        # owners reduce and push their rows to every rank (csrc/peer.cu)
+        chunks, sm_limit = 1, 0
+    else:
+        chunks = MLP_CHUNKS[0] if MLP_CHUNKS[0] > 0 else {1: 1, 2: 1, 4: 2}.get(world, 4)
+        sm_limit = MLP_SM_LIMIT[0] if chunks > 1 else 0
+    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit, comm=comm)
+    if comm == "peer":
+        mlp.attach(dist)
     mlp.fill_synthetic(seed=11)
     jobs = mlp.jobs()
     lanes = chunks > 1
@@ -335,13 +344,13 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     out = {"workload": f"residual MLP block T={T} d={d} ffn={ffn} BF16 (BASELINE configs[3]), tensor parallel x{world}",
            "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
            "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": [x / steps for x in t.job_ms],
-           "row_blocks": chunks, "gemm_sm_limit": sm_limit or None,
+           "row_blocks": chunks, "gemm_sm_limit": sm_limit or None, "collective": comm if world > 1 else None,
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
            "kernels": [k.info.get("impl") for k, _ in jobs], "clocks": clk.summary()}
     if check:
         out["max_err"] = mlp_error(rt, mlp, world, seed=11)
-    if world > 1:
+    if world > 1 and comm == "nccl":
         rt.comm_destroy()
     return out
 
@@ -485,7 +494,51 @@ def mlp_error(rt, mlp, world, seed, rows=(0, 1, 4097, 8191)):
     rms = float(np.sqrt((ref ** 2).mean()))
     return {"rows": len(rows), "max_err_over_m": float((err / mag).max()), "max_err_over_rms": float(err.max() / rms),
             "max_err_over_ref_bf16_ulps": float((err / np.maximum(np.abs(ref), rms * 1e-3)).max() / 2.0 ** -8),
-            "tp": world, "allreduce_dtype": "bf16"}
+            "tp": world, "collective": (MLP_COMM[0] if world > 1 else None),
+            "partials_dtype": "bf16"}
+
+
+def kernel_case(rt, case):
+    """One kernel family on a small synthetic case (inputs above L2 where the
+    kernel is memory-bound), for ncu captures: returns its jobs."""
+    def bufs(*specs):
+        out = []
+        for n, dt in specs:
+            b = rt.alloc(n, dt)
+            rt.fill(b, "uniform", seed=len(out) + 1, stream=len(out), lo=-1, hi=1)
+            out.append(b)
+        return out
+    if case == "tf32_kn":  # TF32 GEMM with B [K,N]: the transpose pass and the tcgen05 GEMM
+        m = 4096
+        a, b, c = bufs((m * m, "tf32"), (m * m, "tf32"), (m * m, "fp32"))
+        return [(rt.compile({"op": "gemm", "m": m, "n": m, "k": m, "tiled": True, "dtype": "tf32"}), [a, b, c])]
+    if case in ("ffma512", "ffma2048"):  # FP32 FFMA GEMM (BASELINE configs[0] and a larger square)
+        m = 512 if case == "ffma512" else 2048
+        a, b, c = bufs((m * m, "fp32"), (m * m, "fp32"), (m * m, "fp32"))
+        return [(rt.compile({"op": "gemm", "m": m, "n": m, "k": m, "tiled": True}), [a, b, c])]
+    if case in ("swiglu", "axpy", "add"):  # FP32 streaming kernels, 2^26 elements
+        n = 1 << 26
+        a, b, c = bufs((n, "fp32"), (n, "fp32"), (n, "fp32"))
+        spec = {"swiglu": {"op": "swi_glu", "len": n}, "axpy": {"op": "axpy", "len": n, "alpha": 0.5},
+                "add": {"op": "add", "len": n}}[case]
+        return [(rt.compile(spec), [a, b, c])]
+    if case == "swiglu_bf16":
+        n = 1 << 27
+        a, b, c = bufs((n, "bf16"), (n, "bf16"), (n, "bf16"))
+        return [(rt.compile({"op": "swi_glu", "len": n, "dtype": "bf16"}), [a, b, c])]
+    if case == "attention_fp32":  # the reference's FP32 online attention (SIMT path), 32 heads x 2048 x 64, causal
+        h, s_, d = 32, 2048, 64
+        q, k, v, o = bufs(*[(h * s_ * d, "fp32")] * 4)
+        return [(rt.compile({"op": "attention_online", "heads": h, "seq": s_, "dim": d, "causal": True}), [q, k, v, o])]
+    if case == "mlp_down_k1792":  # the 8-way tensor-parallel shard's down projection with the residual epilogue
+        T, d, f = 8192, 4096, 1792
+        h, wd, x, y = bufs((T * f, "bf16"), (d * f, "bf16"), (T * d, "bf16"), (T * d, "bf16"))
+        return [(rt.compile({"op": "gemm", "m": T, "n": d, "k": f, "tiled": True, "dtype": "bf16", "b_layout": "nk",
+                             "out_dtype": "bf16", "epilogue": "residual"}), [h, wd, x, y])]
+    raise SystemExit(f"unknown kernel case {case}")
+
+
+KERNEL_CASES = ["tf32_kn", "ffma512", "ffma2048", "swiglu", "axpy", "add", "swiglu_bf16", "attention_fp32", "mlp_down_k1792"]
 
 
 def run_only(args):
@@ -513,6 +566,10 @@ def run_only(args):
             res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks, local)}
         elif w == "sweep":
             res = {"workload": "sweep", "components": sweep(rt, dist, world, rank, args.steps, args.warmup, peaks, local)}
+        elif w in KERNEL_CASES:
+            jobs = kernel_case(rt, w)
+            t = rt.execute(jobs, repeats=args.steps, per_job=True)
+            res = {"workload": w, "impl": [k.info.get("impl") for k, _ in jobs], "ms_per_step": [x / args.steps for x in t.job_ms]}
         else:
             raise SystemExit(f"unknown workload {w}")
         if rank == 0:
@@ -653,12 +710,15 @@ def _main(out_fd):
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--mlp-chunks", type=int, default=MLP_CHUNKS[0],
                     help="row blocks of the tensor-parallel MLP (0: 1 up to 2 GPUs, 2 at 4, 4 at 8)")
+    ap.add_argument("--mlp-comm", choices=["nccl", "peer"], default=MLP_COMM[0],
+                    help="tensor-parallel MLP collective: NCCL all-reduce or NVLink peer scatter/reduce")
     ap.add_argument("--mlp-sm-limit", type=int, default=MLP_SM_LIMIT[0],
                     help="persistent CTAs of the tensor-parallel MLP's GEMMs (0 = one per SM)")
-    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "ffma", "mlp", "rows", "sweep"], default=None,
+    ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "ffma", "mlp", "rows", "sweep"] + KERNEL_CASES,
+                    default=None,
                     help="run one workload alone (profiling), printing its own measurement")
     args = ap.parse_args()
-    MLP_CHUNKS[0], MLP_SM_LIMIT[0] = args.mlp_chunks, args.mlp_sm_limit
+    MLP_CHUNKS[0], MLP_SM_LIMIT[0], MLP_COMM[0] = args.mlp_chunks, args.mlp_sm_limit, args.mlp_comm
     if args.warmup < 3:
         args.warmup = 3
     return run_reference(args) if args.impl == "reference" else run_ours(args)

@@ -144,6 +144,17 @@ JR_API int jr_comm_init(void *ctx, int nranks, int rank, const unsigned char id[
 JR_API int jr_comm_init_all(void **ctxs, int count, uint32_t timeout_ms, char *err, size_t cap);
 JR_API int jr_comm_destroy(void *ctx);
 
+/* Peer memory over NVLink for the collectives that run without NCCL (the gemm
+ * "scatter" epilogue, shard_reduce, shard_gather). No counterpart in the
+ * reference (it has no multi-device code). One process per GPU: every rank
+ * exports the buffer with jr_peer_handle, the host gathers the 64-byte handles
+ * in rank order, and every rank calls jr_peer_attach with all of them; each
+ * rank's buffer must have the same size. nranks 1..8; with nranks 1 no handle is
+ * opened. The mappings close when the context is destroyed. */
+JR_API int jr_peer_handle(void *ctx, const void *ptr, unsigned char handle[64], char *err, size_t cap);
+JR_API int jr_peer_attach(void *ctx, const void *ptr, const unsigned char *handles, int nranks, int rank, char *err,
+                          size_t cap);
+
 /* Allocation-free TF32 GEMM: out[m,n] (FP32) = a[m,k] . b[k,n], a and b FP32
  * row-major, computed on the tensor cores in TF32 with FP32 accumulation - the
  * same kernels as a compiled {"op":"gemm","dtype":"tf32"} spec with the default

@@ -22,6 +22,7 @@
 #include <cuda.h>
 
 #include <climits>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 #include <type_traits>
@@ -39,7 +40,7 @@ constexpr uint32_t kStageA = BM * 128, kStageB = BN * 128, kStageBytes = kStageA
 constexpr uint32_t kEpiBlock = 32 * 33 * 4, kEpiBytes = 4 * kEpiBlock;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 256 /*barriers*/ + kEpiBytes + 1024 /*align*/;
 
-enum Epi { kEpiNone = 0, kEpiSwiglu = 1, kEpiResidual = 2 };
+enum Epi { kEpiNone = 0, kEpiSwiglu = 1, kEpiResidual = 2, kEpiScatter = 3 };
 
 struct GemmArgs {
     void *out;
@@ -47,14 +48,32 @@ struct GemmArgs {
     const void *residual;
     int M, N, K;  // N = output columns
     int tiles_m, tiles_n, num_tiles, kblocks;
+    int group_m;  // M-blocks per raster group (tile_coords)
     int *err;
+    // scatter epilogue: every rank's receive buffer; the rows of rank r are
+    // [r * rows_per_rank, (r + 1) * rows_per_rank), this GEMM's rank is my_rank
+    void *scatter[kMaxPeerRanks];
+    int rows_per_rank, my_rank;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
-    constexpr int kGroup = 8;
-    const int per_group = kGroup * tiles_n;
-    const int g = t / per_group, first_m = g * kGroup;
-    const int gm = min(tiles_m - first_m, kGroup);
+// M-blocks per raster group: as many as keep the group's A rows (group x 128 x K
+// elements) within 48 MB of L2, between 8 and 32 (the MLP gate/up GEMM, K = 4096,
+// measured 10% faster at 24-32 than at 8; 64 was slower again), at most all of
+// them; JADE_GEMM_GROUP_M overrides (read when a kernel is compiled).
+int raster_group(int tiles_m, uint64_t k, int eb) {
+    if (const char *force = std::getenv("JADE_GEMM_GROUP_M"); force && *force) return std::max(1, std::min(tiles_m, std::atoi(force)));
+    const uint64_t fit = (48ull << 20) / ((uint64_t)BM * k * eb);
+    return (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)tiles_m, std::min<uint64_t>(32, std::max<uint64_t>(8, fit))));
+}
+
+// Tile t of the grouped raster: M-blocks in groups of `group` rows, every N-block
+// of a group before the next group, M fastest inside a group. A group's A rows
+// stay in L2 while its N-blocks stream past, so B is read from DRAM about
+// tiles_m / group times and A about once.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int &tm, int &tn) {
+    const int per_group = group * tiles_n;
+    const int g = t / per_group, first_m = g * group;
+    const int gm = min(tiles_m - first_m, group);
     const int r = t % per_group;
     tm = first_m + r % gm;
     tn = r / gm;
@@ -225,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t last_phase[kStages] = {};
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
                 int tm, tn;
-                tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+                tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
                 const int m0 = tm * BM, nb0 = tn * BN;  // B rows (nk) or columns (kn) of this tile
                 for (int kb = 0; kb < args.kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
@@ -293,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ResidualChunk<TOut> res_next;
         for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
             int tm, tn;
-            tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+            tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
             if constexpr (kEpi == kEpiResidual)  // the residual does not wait for the MMAs: fetch chunk 0 now
                 load_residual(res_next, static_cast<const TOut *>(args.residual), tm * BM + quarter * 32, r_sub, tn * BN + c_sub,
                               args.M, args.N, (args.N % 4) == 0);
@@ -303,6 +322,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
             const float scale = (kRowScale && row < args.M) ? args.row_scale[row] : 1.0f;
             TOut *out = static_cast<TOut *>(args.out);
+            if constexpr (kEpi == kEpiScatter) {
+                // the tile's rows belong to one rank: its receive buffer, this rank's slot
+                const int owner = (tm * BM) / args.rows_per_rank;
+                out = static_cast<TOut *>(args.scatter[owner]) + (ptrdiff_t)(args.my_rank - owner) * args.rows_per_rank * args.N;
+            }
             if constexpr (kEpi == kEpiSwiglu) {
                 const int c0 = tn * 128;
 #pragma unroll 1
@@ -419,8 +443,14 @@ LaunchFn tc_launch(Context *ctx, const Spec &s) {
     base.tiles_n = swiglu ? (int)(s.n / 128) : (int)((s.n + BN - 1) / BN);
     base.num_tiles = base.tiles_m * base.tiles_n;
     base.kblocks = (int)((s.k + (128 / kEB) - 1) / (128 / kEB));
+    base.group_m = raster_group(base.tiles_m, s.k, kEB);
     base.err = ctx->err_dev;
     const int grid = std::min(base.num_tiles, s.sm_limit ? std::min<int>((int)s.sm_limit, ctx->sm_count) : ctx->sm_count);
+    const uint32_t ranks = s.ranks, rank = s.rank;
+    if (kEpi == kEpiScatter) {
+        base.rows_per_rank = (int)(s.m / s.ranks);
+        base.my_rank = (int)s.rank;
+    }
     const uint64_t M = s.m, K = s.k;
     return [=](cudaStream_t st, void **b) {
         CUtensorMap ma, mb;
@@ -433,13 +463,26 @@ LaunchFn tc_launch(Context *ctx, const Spec &s) {
         a.row_scale = kRowScale ? static_cast<const float *>(b[idx++]) : nullptr;
         a.residual = kEpi == kEpiResidual ? b[idx++] : nullptr;
         a.out = b[idx];
+        PeerSet flags{};
+        if constexpr (kEpi == kEpiScatter) {
+            PeerSet recv{};
+            if (!find_peers(ctx, b[idx], ranks, recv) || !find_peers(ctx, b[idx + 1], ranks, flags)) return cudaErrorInvalidResourceHandle;
+            for (uint32_t q = 0; q < kMaxPeerRanks; ++q) a.scatter[q] = recv.p[q];
+        }
         kernel<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, a);
-        return cudaGetLastError();
+        cudaError_t e = cudaGetLastError();
+        if constexpr (kEpi == kEpiScatter)  // phase 0: this rank's partial rows are in their owners' buffers
+            if (e == cudaSuccess) e = launch_peer_signal(st, flags, ranks, rank, 0);
+        return e;
     };
 }
 
 template <int kEB, uint32_t kFmt, typename TOut, typename T16>
 LaunchFn pick_epilogue(Context *ctx, const Spec &s) {
+    if (s.epilogue == "scatter") {
+        if constexpr (!std::is_same<TOut, float>::value) return tc_launch<kEB, kFmt, false, TOut, kEpiScatter, false>(ctx, s);
+        throw IrError("scatter epilogue needs a 16-bit output");
+    }
     if (s.epilogue == "swiglu") {
         if (s.row_scale) return tc_launch<kEB, kFmt, false, TOut, kEpiSwiglu, true>(ctx, s);
         return tc_launch<kEB, kFmt, false, TOut, kEpiSwiglu, false>(ctx, s);
@@ -636,6 +679,7 @@ extern "C" JR_API int jr_gemm_tf32_kn_noalloc(const float *a, const float *b, fl
     args.tiles_n = (int)((n + BN - 1) / BN);
     args.num_tiles = args.tiles_m * args.tiles_n;
     args.kblocks = (int)((k + 31) / 32);
+    args.group_m = 8;
     args.err = d->err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // B [K,N] -> scratch [N,K]: the whole K*N region is rewritten, nothing needs clearing.

@@ -40,6 +40,11 @@ struct Context {
     uint32_t comm_timeout_ms = 60000;
     // cuBLAS handle for the gemm_mps library comparator (lazy)
     void *cublas = nullptr;
+    // peer memory (jr_peer_attach): a local buffer -> every rank's device address
+    // of its counterpart (this rank's own entry is the buffer itself), and the
+    // mappings this context opened
+    std::map<uintptr_t, std::vector<void *>> peers;
+    std::vector<void *> ipc_opened;
     // runtime-compiled elementwise modules, keyed by full source text
     std::map<std::string, std::pair<void *, void *>> rtc_modules;  // source -> (CUmodule, CUfunction)
     std::mutex rtc_mutex;
@@ -56,6 +61,8 @@ struct jr_kernel {
     std::string impl;  // implementation name reported by jr_kernel_info
     std::string path;  // "tcgen05", "simt", "nvrtc", "nccl", "copy", "cublas"
     bool collective = false;
+    std::vector<size_t> peer_bindings;  // bindings that must be attached peer buffers (ranks entries)
+    uint32_t peer_ranks = 0;
     jade::LaunchFn run;
 };
 
@@ -95,6 +102,15 @@ LaunchFn make_elementwise_rtc(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_misc_kernel(Context *ctx, const Spec &s, std::string &impl);  // fill, l2_flush
 LaunchFn make_cublas_gemm(Context *ctx, const Spec &s, std::string &impl);
 LaunchFn make_all_reduce(Context *ctx, const Spec &s, std::string &impl);
+// Peer collectives over NVLink (peer.cu): shard_reduce and shard_gather, and the
+// arrival signal the gemm "scatter" epilogue sends after its stores.
+LaunchFn make_shard_op(Context *ctx, const Spec &s, std::string &impl);
+struct PeerSet {
+    void *p[kMaxPeerRanks];
+};
+PeerSet peer_set(Context *ctx, const void *local, uint32_t ranks);  // throws if not attached
+bool find_peers(Context *ctx, const void *local, uint32_t ranks, PeerSet &out);
+cudaError_t launch_peer_signal(cudaStream_t st, const PeerSet &flags, uint32_t ranks, uint32_t rank, int phase);
 void cublas_destroy(Context *ctx);
 void rtc_destroy(Context *ctx);
 void comm_destroy(Context *ctx);

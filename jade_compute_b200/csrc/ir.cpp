@@ -146,7 +146,8 @@ DType parse_dtype(const std::string &s) {
 
 bool Spec::extended() const {
     return has_dtype || has_out_dtype || has_batch || has_b_layout || epilogue != "none" || row_scale || sm_limit ||
-           op == Op::RmsInv || op == Op::AllReduce || op == Op::Copy || op == Op::L2Flush || op == Op::Fill || op == Op::WaitProbe;
+           op == Op::RmsInv || op == Op::AllReduce || op == Op::Copy || op == Op::L2Flush || op == Op::Fill || op == Op::WaitProbe ||
+           op == Op::ShardReduce || op == Op::ShardGather || ranks;
 }
 
 const char *spec_name(const Spec &s) {
@@ -168,6 +169,8 @@ const char *spec_name(const Spec &s) {
         case Op::Copy: return "copy";
         case Op::L2Flush: return "l2_flush";
         case Op::WaitProbe: return "wait_probe";
+        case Op::ShardReduce: return "shard_reduce";
+        case Op::ShardGather: return "shard_gather";
         case Op::Fill: return "fill";
     }
     return "?";
@@ -208,6 +211,11 @@ Spec parse_spec(const Json &j) {
     else if (op == "copy") { s.op = Op::Copy; s.bytes = get_uint(j, "bytes", UINT64_MAX); s.direction = get_str(j, "direction"); }
     else if (op == "l2_flush") { s.op = Op::L2Flush; s.bytes = get_uint(j, "bytes", UINT64_MAX); }
     else if (op == "wait_probe") { s.op = Op::WaitProbe; s.limit_ns = get_uint(j, "limit_ns", UINT64_MAX); }
+    else if (op == "shard_reduce" || op == "shard_gather") {
+        s.op = op == "shard_reduce" ? Op::ShardReduce : Op::ShardGather;
+        s.rows = get_u32(j, "rows"); s.cols = get_u32(j, "cols");
+        if (j.has("residual")) s.residual = get_bool(j, "residual");
+    }
     else if (op == "fill") {
         s.op = Op::Fill; s.len = get_u32(j, "len"); s.dist = get_str(j, "dist");
         s.seed = get_uint(j, "seed", UINT64_MAX);
@@ -218,7 +226,7 @@ Spec parse_spec(const Json &j) {
     } else {
         bail("unknown variant `" + op + "`, expected one of `elementwise`, `axpy`, `add`, `gemm`, `gemm_simd`, `gemm_mps`, "
              "`attention_scores`, `attention_apply`, `attention_online`, `rms_norm`, `swi_glu`, `softmax`, "
-             "`rms_inv`, `all_reduce`, `copy`, `l2_flush`, `fill`, `wait_probe`");
+             "`rms_inv`, `all_reduce`, `copy`, `l2_flush`, `fill`, `wait_probe`, `shard_reduce`, `shard_gather`");
     }
     if (const Json *d = j.get("dtype")) {
         if (d->kind != Json::String) bail("invalid type for `dtype`");
@@ -244,6 +252,8 @@ Spec parse_spec(const Json &j) {
     }
     if (j.has("row_scale")) s.row_scale = get_bool(j, "row_scale");
     if (j.has("sm_limit")) s.sm_limit = get_u32(j, "sm_limit");
+    if (j.has("ranks")) s.ranks = get_u32(j, "ranks");
+    if (j.has("rank")) s.rank = get_u32(j, "rank");
     return s;
 }
 
@@ -280,6 +290,10 @@ Json spec_to_json(const Spec &s) {
         case Op::Copy: j.set("op", Json::str("copy")).set("bytes", U(s.bytes)).set("direction", Json::str(s.direction)); break;
         case Op::L2Flush: j.set("op", Json::str("l2_flush")).set("bytes", U(s.bytes)); break;
         case Op::WaitProbe: j.set("op", Json::str("wait_probe")).set("limit_ns", U(s.limit_ns)); break;
+        case Op::ShardReduce: case Op::ShardGather:
+            j.set("op", Json::str(s.op == Op::ShardReduce ? "shard_reduce" : "shard_gather")).set("rows", U(s.rows)).set("cols", U(s.cols));
+            if (s.residual) j.set("residual", Json::boolean(true));
+            break;
         case Op::Fill:
             j.set("op", Json::str("fill")).set("len", U(s.len)).set("dist", Json::str(s.dist)).set("seed", U(s.seed))
                 .set("stream", U(s.stream_id)).set("lo", Json::f32(s.lo)).set("hi", Json::f32(s.hi));
@@ -293,6 +307,7 @@ Json spec_to_json(const Spec &s) {
     if (s.epilogue != "none") j.set("epilogue", Json::str(s.epilogue));
     if (s.row_scale) j.set("row_scale", Json::boolean(true));
     if (s.sm_limit) j.set("sm_limit", U(s.sm_limit));
+    if (s.ranks) j.set("ranks", U(s.ranks)).set("rank", U(s.rank));
     return j;
 }
 
@@ -323,8 +338,15 @@ void validate(const Spec &s) {  // ir.rs:193-268 plus the extensions
                    "gemm out_dtype must be fp32 or the 16-bit input type");
             if (s.epilogue != "none" || s.row_scale || s.b_nk || s.sm_limit)
                 ensure(s.dtype != DType::F32, "GEMM fusion, b_layout nk and sm_limit need a tensor-core dtype (tf32, bf16, fp16)");
-            ensure(s.epilogue == "none" || s.epilogue == "swiglu" || s.epilogue == "residual",
-                   "epilogue must be none, swiglu or residual");
+            ensure(s.epilogue == "none" || s.epilogue == "swiglu" || s.epilogue == "residual" || s.epilogue == "scatter",
+                   "epilogue must be none, swiglu, residual or scatter");
+            ensure((s.epilogue == "scatter") == (s.ranks > 0), "the scatter epilogue and ranks go together");
+            if (s.epilogue == "scatter") {
+                ensure(is16(s.dtype) && s.out_dtype == s.dtype && s.b_nk && !s.row_scale,
+                       "scatter epilogue needs 16-bit inputs and outputs of the same type and b_layout nk");
+                ensure(s.ranks <= kMaxPeerRanks && s.rank < s.ranks, "ranks must be 1..8 and rank below it");
+                ensure(s.m % (128 * s.ranks) == 0, "scatter epilogue needs m to be a multiple of 128 * ranks");
+            }
             if (s.epilogue == "swiglu") {
                 ensure(is16(s.dtype) && s.b_nk, "swiglu epilogue needs 16-bit inputs and b_layout nk");
                 ensure(s.n % 128 == 0, "swiglu epilogue needs n to be a multiple of 128");
@@ -367,6 +389,14 @@ void validate(const Spec &s) {  // ir.rs:193-268 plus the extensions
         case Op::WaitProbe:
             ensure(s.limit_ns >= 1000 && s.limit_ns <= 10000000000ull, "wait_probe limit_ns must be 1e3..1e10");
             break;
+        case Op::ShardReduce: case Op::ShardGather:
+            matrix(s.rows, s.cols);
+            check_dtype(s, {DType::BF16});
+            ensure(s.ranks >= 1 && s.ranks <= kMaxPeerRanks && s.rank < s.ranks, "ranks must be 1..8 and rank below it");
+            ensure(s.rows % s.ranks == 0, "rows must split evenly over the ranks");
+            ensure(s.cols % 8 == 0, "cols must be a multiple of 8 (16-byte rows)");
+            ensure(s.op == Op::ShardReduce || !s.residual, "residual applies to shard_reduce");
+            break;
         case Op::Fill:
             dim(s.len);
             ensure(s.dist == "uniform" || s.dist == "normal", "fill dist must be uniform or normal");
@@ -376,6 +406,8 @@ void validate(const Spec &s) {  // ir.rs:193-268 plus the extensions
     }
     if (s.op != Op::Gemm) {
         ensure(!s.has_b_layout && s.epilogue == "none" && !s.row_scale, std::string(spec_name(s)) + " has no GEMM fusion fields");
+        ensure(!s.ranks || s.op == Op::ShardReduce || s.op == Op::ShardGather,
+               std::string(spec_name(s)) + " has no ranks (gemm scatter and the shard collectives only)");
     }
     if (s.has_batch) ensure(s.op == Op::AttentionOnline || s.op == Op::AttentionScores || s.op == Op::AttentionApply, "batch applies to attention only");
 }
@@ -403,6 +435,7 @@ std::vector<Binding> bindings(const Spec &s) {  // ir.rs:269-339
             if (s.row_scale) r.push_back(b("row_scale", s.m, false, DType::F32));
             if (s.epilogue == "residual") r.push_back(b("residual", (uint64_t)s.m * s.n, false, s.out_dtype));
             r.push_back(b("out", (uint64_t)s.m * s.n, true, s.out_dtype));
+            if (s.epilogue == "scatter") r.push_back(b("flags", kPeerFlagBytes, true, DType::U8));
             break;
         }
         case Op::AttentionScores: {
@@ -435,6 +468,17 @@ std::vector<Binding> bindings(const Spec &s) {  // ir.rs:269-339
         }
         case Op::L2Flush: r = {b("scratch", s.bytes, true, DType::U8)}; break;
         case Op::WaitProbe: r = {b("elapsed_ns", 2, true, DType::F32)}; break;
+        case Op::ShardReduce: {
+            const uint64_t n = (uint64_t)s.rows * s.cols;
+            r = {b("partials", n, false, d)};
+            if (s.residual) r.push_back(b("residual", n, false, d));
+            r.push_back(b("out", n, true, d));
+            r.push_back(b("flags", kPeerFlagBytes, true, DType::U8));
+            break;
+        }
+        case Op::ShardGather:
+            r = {b("out", (uint64_t)s.rows * s.cols, true, d), b("flags", kPeerFlagBytes, true, DType::U8)};
+            break;
         case Op::Fill: r = {b("out", s.len, true, d)}; break;
     }
     return r;

@@ -43,8 +43,13 @@ struct Expr {
 enum class Op {
     Elementwise, Axpy, Add, Gemm, GemmSimd, GemmMps, AttentionScores, AttentionApply,
     AttentionOnline, RmsNorm, SwiGlu, Softmax,
-    RmsInv, AllReduce, Copy, L2Flush, Fill, WaitProbe
+    RmsInv, AllReduce, Copy, L2Flush, Fill, WaitProbe, ShardReduce, ShardGather
 };
+
+// Words of the per-rank flag buffer that the peer collectives share (arrivals
+// per rank for two phases, two local epoch counters), as bytes.
+constexpr uint32_t kPeerFlagBytes = 256;
+constexpr uint32_t kMaxPeerRanks = 8;
 
 struct Spec {
     Op op = Op::Add;
@@ -73,6 +78,8 @@ struct Spec {
     uint64_t offset = 0;    // fill: generator index of element 0 (a slice of a larger fill)
     uint32_t sm_limit = 0;  // tcgen05 gemm: at most this many persistent CTAs (0 = one per SM)
     uint64_t limit_ns = 0;  // wait_probe: the bounded wait's time limit
+    uint32_t ranks = 0, rank = 0;  // peer collectives and the gemm "scatter" epilogue
+    bool residual = false;         // shard_reduce: add a residual to the reduced rows
     bool extended() const;
 };
 

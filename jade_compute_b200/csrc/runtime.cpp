@@ -66,6 +66,9 @@ void teardown(Context *ctx) {
     jade::comm_destroy(ctx);
     jade::cublas_destroy(ctx);
     jade::rtc_destroy(ctx);
+    for (void *p : ctx->ipc_opened) cudaIpcCloseMemHandle(p);
+    ctx->ipc_opened.clear();
+    ctx->peers.clear();
     for (const auto &entry : ctx->allocations) {
         void *p = reinterpret_cast<void *>(entry.first);
         if (entry.second.host) cudaFreeHost(p);
@@ -386,6 +389,10 @@ void select_implementation(Context *ctx, jr_kernel &k) {
             if (s.op == Op::Gemm && s.dtype != jade::DType::F32 && jade::gemm_tc_supports(s, why)) {
                 k.run = jade::make_gemm_tc(ctx, s, k.impl);
                 k.path = "tcgen05";
+                if (s.epilogue == "scatter") {  // out (the local receive buffer) and flags
+                    k.peer_ranks = s.ranks;
+                    k.peer_bindings = {k.binds.size() - 2, k.binds.size() - 1};
+                }
             } else {
                 k.run = jade::make_gemm_simt(ctx, s, k.impl);
                 k.path = "simt";
@@ -417,6 +424,13 @@ void select_implementation(Context *ctx, jr_kernel &k) {
             k.run = jade::make_all_reduce(ctx, s, k.impl);
             k.path = "nccl";
             k.collective = true;
+            return;
+        case Op::ShardReduce: case Op::ShardGather:
+            k.run = jade::make_shard_op(ctx, s, k.impl);
+            k.path = "nvlink";
+            k.peer_ranks = s.ranks;
+            if (s.op == Op::ShardReduce) k.peer_bindings = {s.residual ? 2u : 1u, s.residual ? 3u : 2u};  // out, flags
+            else k.peer_bindings = {1};                                                                   // flags
             return;
         case Op::Copy: {
             const cudaMemcpyKind kind = s.direction == "h2d"   ? cudaMemcpyHostToDevice
@@ -494,6 +508,12 @@ void check_batch(Context &ctx, const jr_dispatch *jobs, size_t n) {
                       (unsigned long long)want, (unsigned long long)bind.elements, jade::dtype_name(bind.dtype), reg->second.bytes);
             if (bind.write && std::count(d.buffers, d.buffers + binds.size(), p) > 1)
                 raise(JR_EINVAL, "job %zu: output binding must not alias another binding", j);
+        }
+        for (size_t b : d.kernel->peer_bindings) {
+            const auto peer = ctx.peers.find(reinterpret_cast<uintptr_t>(d.buffers[b]));
+            if (peer == ctx.peers.end() || peer->second.size() != d.kernel->peer_ranks)
+                raise(JR_EINVAL, "job %zu: buffer %s is not attached to peer memory of %u ranks (jr_peer_attach)", j, binds[b].name.c_str(),
+                      d.kernel->peer_ranks);
         }
     }
 }

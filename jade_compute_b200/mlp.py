@@ -65,13 +65,15 @@ class ResidualMLP:
     collective's kernels find free SMs beside them."""
 
     def __init__(self, rt: Runtime, tokens: int, width: int, hidden: int, tp: int = 1, rank: int = 0,
-                 eps: float = 1e-5, collective: bool = True, chunks: int = 1, sm_limit: int = 0):
+                 eps: float = 1e-5, collective: bool = True, chunks: int = 1, sm_limit: int = 0, comm: str = "nccl"):
         self.rt, self.T, self.d, self.ffn, self.tp, self.rank, self.eps = rt, tokens, width, hidden, tp, rank, eps
         self.f = hidden // tp
         shard_columns(hidden, tp, rank)
         if chunks < 1 or tokens % chunks:
             raise ValueError(f"tokens={tokens} must split into {chunks} equal row blocks")
-        self.chunks, self.Tc = chunks, tokens // chunks
+        if comm not in ("nccl", "peer"):
+            raise ValueError("comm must be nccl or peer")
+        self.chunks, self.Tc, self.comm = chunks, tokens // chunks, comm
         Tc, d, f = self.Tc, width, self.f
         self.xs = [rt.alloc(Tc * d, "bf16") for _ in range(chunks)]
         self.invs = [rt.alloc(Tc, "fp32") for _ in range(chunks)]
@@ -85,10 +87,31 @@ class ResidualMLP:
         self.k_inv = rt.compile({"op": "rms_inv", "rows": Tc, "cols": d, "epsilon": eps, "dtype": "bf16"})
         self.k_up = rt.compile({"op": "gemm", "m": Tc, "n": f, "k": d, "epilogue": "swiglu", "row_scale": True, **base})
         down = {"op": "gemm", "m": Tc, "n": d, "k": f, **base}
-        if rank == 0:
-            down["epilogue"] = "residual"
+        self.k_ar = self.k_reduce = self.k_gather = None
+        if comm == "peer":
+            # the down GEMM stores its partial rows straight into their owners'
+            # receive buffers; each owner sums its rows (+ x) and stores them into
+            # every rank's y (csrc/peer.cu)
+            down.update({"epilogue": "scatter", "ranks": tp, "rank": rank})
+            shard = {"rows": Tc, "cols": d, "ranks": tp, "rank": rank, "dtype": "bf16"}
+            self.k_reduce = rt.compile({"op": "shard_reduce", "residual": True, **shard})
+            self.k_gather = rt.compile({"op": "shard_gather", **shard})
+            self.recvs = [rt.alloc(Tc * d, "bf16") for _ in range(chunks)]
+            self.flags = rt.alloc_bytes(256)
+        else:
+            if rank == 0:
+                down["epilogue"] = "residual"
+            if tp > 1 and collective:
+                self.k_ar = rt.compile({"op": "all_reduce", "len": Tc * d, "dtype": "bf16"})
         self.k_down = rt.compile(down)
-        self.k_ar = rt.compile({"op": "all_reduce", "len": Tc * d, "dtype": "bf16"}) if tp > 1 and collective else None
+
+    def attach(self, dist) -> None:
+        """Peer mode: maps the receive buffers, outputs and flags of every rank
+        (a collective call: every rank of the block calls it)."""
+        from .parallel import share_buffers
+        if self.comm != "peer":
+            raise ValueError("attach is for comm='peer'")
+        share_buffers(self.rt, dist, [*self.recvs, *self.ys, self.flags])
 
     # single-block views (chunks == 1)
     @property
@@ -105,10 +128,15 @@ class ResidualMLP:
 
     def jobs(self):
         j = []
-        for x, inv, h, y in zip(self.xs, self.invs, self.hs, self.ys):
-            j += [(self.k_inv, [x, inv]),
-                  (self.k_up, [x, self.wgu, inv, h]),
-                  (self.k_down, [h, self.wd, x, y] if self.rank == 0 else [h, self.wd, y])]
+        for c, (x, inv, h, y) in enumerate(zip(self.xs, self.invs, self.hs, self.ys)):
+            j += [(self.k_inv, [x, inv]), (self.k_up, [x, self.wgu, inv, h])]
+            if self.comm == "peer":
+                recv = self.recvs[c]
+                j += [(self.k_down, [h, self.wd, recv, self.flags]),
+                      (self.k_reduce, [recv, x, y, self.flags]),
+                      (self.k_gather, [y, self.flags])]
+                continue
+            j.append((self.k_down, [h, self.wd, x, y] if self.rank == 0 else [h, self.wd, y]))
             if self.k_ar is not None:
                 j.append((self.k_ar, [y]))
         return j

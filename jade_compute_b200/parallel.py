@@ -75,3 +75,25 @@ def init_comm(rt: "_rt.Runtime", dist, timeout_ms: int = 60000,
     uid = make_id() if rank == 0 else None
     uid = broadcast_bytes(dist, uid, src=0, size=128)
     rt.comm_init(world, rank, uid, timeout_ms)
+
+
+def all_gather_bytes(dist, payload: bytes) -> list:
+    """Every rank's fixed-size byte string, in rank order, over the CPU group."""
+    import torch
+    world = dist.get_world_size()
+    mine = torch.frombuffer(bytearray(payload), dtype=torch.uint8)
+    out = [torch.zeros(len(payload), dtype=torch.uint8) for _ in range(world)]
+    dist.all_gather(out, mine)
+    return [bytes(t.tolist()) for t in out]
+
+
+def share_buffers(rt: "_rt.Runtime", dist, buffers) -> None:
+    """Attaches each buffer to its counterparts on every rank (CUDA IPC handles
+    exchanged over the CPU group; every rank passes the same sequence of
+    same-sized buffers). Single process: attaches with one rank."""
+    rank = dist.get_rank() if dist is not None else 0
+    for buf in buffers:
+        handles = all_gather_bytes(dist, rt.peer_handle(buf)) if dist is not None else [b"\0" * 64]
+        rt.peer_attach(buf, handles, rank)
+    if dist is not None:
+        dist.barrier()

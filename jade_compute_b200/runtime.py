@@ -90,6 +90,8 @@ def lib() -> ctypes.CDLL:
     L.jr_comm_init.argtypes = [vp, i32, i32, ctypes.c_char_p, u32, c_char_p, sz]
     L.jr_comm_init_all.argtypes = [ctypes.POINTER(vp), i32, u32, c_char_p, sz]
     L.jr_comm_destroy.argtypes = [vp]
+    L.jr_peer_handle.argtypes = [vp, vp, ctypes.c_char_p, c_char_p, sz]
+    L.jr_peer_attach.argtypes = [vp, vp, ctypes.c_char_p, i32, i32, c_char_p, sz]
     _lib = L
     return L
 
@@ -389,6 +391,22 @@ class Runtime:
         self.execute([(k, [buf])])
         k.release()
         self._kernels.remove(k)
+
+    # -- peer memory (collectives over NVLink without NCCL)
+    def peer_handle(self, buf: Buffer) -> bytes:
+        """The 64-byte CUDA IPC handle of a device buffer, for the other ranks."""
+        self._own(buf)
+        out = ctypes.create_string_buffer(64)
+        e = _err()
+        _check(lib().jr_peer_handle(self.ctx, buf.ptr, out, e, len(e)), e)
+        return out.raw
+
+    def peer_attach(self, buf: Buffer, handles: Sequence[bytes], rank: int) -> None:
+        """Maps every other rank's counterpart of `buf` (handles in rank order)."""
+        self._own(buf)
+        blob = b"".join(handles)
+        e = _err()
+        _check(lib().jr_peer_attach(self.ctx, buf.ptr, blob, len(handles), rank, e, len(e)), e)
 
     # -- collectives
     def comm_init(self, nranks: int, rank: int, unique_id: bytes, timeout_ms: int = 60000) -> None:

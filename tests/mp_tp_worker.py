@@ -14,7 +14,7 @@ from jade_compute_b200 import parallel  # noqa: E402
 from jade_compute_b200.mlp import ResidualMLP  # noqa: E402
 
 
-def main(out_dir):
+def main(out_dir, comm="nccl"):
     rank, world, local = parallel.env_ranks()
     dist = parallel.init_process_group(timeout_s=120)
     rt = jc.Runtime(local)
@@ -25,11 +25,18 @@ def main(out_dir):
     norm = rng.uniform(0.5, 1.5, d).astype(np.float32)
     wg, wu = ((rng.standard_normal((d, ffn)) * 0.05).astype(np.float32) for _ in range(2))
     wd = (rng.standard_normal((ffn, d)) * 0.05).astype(np.float32)
-    # two row blocks: block 0's all-reduce runs on the collective stream beside
-    # block 1's GEMMs
-    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=2, sm_limit=120)
-    mlp.load(x, norm, wg, wu, wd)
-    rt.execute(mlp.jobs(), repeats=2, streams=True)
+    if comm == "peer":
+        # partials scattered to their owners over NVLink, reduced and pushed back
+        mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, comm="peer")
+        mlp.attach(dist)
+        mlp.load(x, norm, wg, wu, wd)
+        rt.execute(mlp.jobs(), repeats=3)
+    else:
+        # two row blocks: block 0's all-reduce runs on the collective stream beside
+        # block 1's GEMMs
+        mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=2, sm_limit=120)
+        mlp.load(x, norm, wg, wu, wd)
+        rt.execute(mlp.jobs(), repeats=2, streams=True)
     np.save(os.path.join(out_dir, f"y_{rank}.npy"), mlp.download_y())
     dist.barrier()
     rt.comm_destroy()
@@ -38,4 +45,4 @@ def main(out_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1])
+    main(sys.argv[1], *sys.argv[2:])

@@ -17,6 +17,7 @@
    the unsharded block (the all-reduce itself is covered by the multi-GPU test);
    each BF16 partial adds its own rounding, 2^-8 |partial|.
 """
+import json
 import math
 
 import numpy as np
@@ -169,3 +170,27 @@ def test_row_blocks_and_collective_lane_give_the_same_bits(rt):
     assert np.array_equal(whole.download_y(), blocks.download_y())
     rows = np.array([0, 255, 256, 1023])
     assert np.array_equal(blocks.download_y_rows(rows), whole.download_y().reshape(T, d)[rows])
+
+
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_peer_collective_path_on_one_rank(rt, chunks):
+    # comm="peer" with one rank: the down GEMM's scatter epilogue, shard_reduce (+x)
+    # and shard_gather run their whole data path on one GPU (the arrival flags are
+    # this rank's own). The partial is rounded to BF16 before the reduction adds x,
+    # one rounding more than the residual epilogue: 2^-8 |partial| more slack.
+    T, d, ffn = 1024, 512, 1024
+    ref = ResidualMLP(rt, T, d, ffn)
+    peer = ResidualMLP(rt, T, d, ffn, comm="peer", chunks=chunks)
+    peer.attach(None)
+    assert "scatter" in peer.k_down.info["impl"] or "scatter" in json.dumps(peer.k_down.spec)
+    for m in (ref, peer):
+        m.fill_synthetic(seed=8)
+    rt.execute(ref.jobs())
+    rt.execute(peer.jobs(), repeats=3)  # arrival numbers advance every repeat
+    first = peer.download_y()
+    rt.execute(peer.jobs(), repeats=2, graph=True)  # the epochs live on the device: graphs replay too
+    assert np.array_equal(peer.download_y(), first)
+    rows = np.arange(0, T, 37)
+    oracle = effective_oracle(rt, [peer], rows)
+    partial = np.abs(oracle[0] - peer.download_x().reshape(T, d)[rows])
+    check_mlp(first.reshape(T, d)[rows], oracle, ffn, extra=2.0 ** -8 * partial)

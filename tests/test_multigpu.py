@@ -19,10 +19,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.skipif(jc.device_count() < 2 if os.path.exists(jc.library_path()) else True, reason="needs 2 GPUs")
-def test_tensor_parallel_mlp_all_reduce_two_gpus(tmp_path):
+@pytest.mark.parametrize("comm", ["nccl", "peer"])
+def test_tensor_parallel_mlp_all_reduce_two_gpus(tmp_path, comm):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
+    port = "29533" if comm == "nccl" else "29534"
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(HERE, "mp_tp_worker.py"), str(tmp_path)]
+           "--master-addr=127.0.0.1", f"--master-port={port}", os.path.join(HERE, "mp_tp_worker.py"), str(tmp_path), comm]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     y0, y1 = np.load(tmp_path / "y_0.npy"), np.load(tmp_path / "y_1.npy")
