@@ -348,6 +348,16 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
            "kernels": [k.info.get("impl") for k, _ in jobs], "clocks": clk.summary()}
+    if world > 1:
+        # time of the collective jobs per block (all row blocks), and for the NCCL
+        # all-reduce its bus bandwidth: 2 (N-1)/N x bytes / time
+        job_ms = [x / steps for x in t.job_ms]
+        if comm == "nccl":
+            coll_ms = sum(ms_ for (k, _), ms_ in zip(jobs, job_ms) if k is mlp.k_ar)
+            out["collective_ms"] = coll_ms
+            out["allreduce_busbw_gbs"] = 2 * (world - 1) / world * T * d * 2 / (coll_ms * 1e-3) / 1e9 if coll_ms else None
+        else:
+            out["collective_ms"] = sum(ms_ for (k, _), ms_ in zip(jobs, job_ms) if k in (mlp.k_reduce, mlp.k_gather))
     if check:
         out["max_err"] = mlp_error(rt, mlp, world, seed=11)
     if world > 1 and comm == "nccl":
