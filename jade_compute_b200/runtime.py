@@ -21,7 +21,9 @@ from typing import Iterable, Sequence
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libjade_runtime.so")
+# JADE_RUNTIME_LIBRARY selects another build of this library (e.g. a variant
+# compiled with different options); by default the in-tree build.
+LIB_PATH = os.environ.get("JADE_RUNTIME_LIBRARY") or os.path.join(HERE, "lib", "libjade_runtime.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include", "jade_runtime.h")
 
 JR_OK, JR_EINVAL, JR_ECUDA, JR_ENOMEM, JR_ETIMEOUT = 0, 1, 2, 3, 4
