@@ -12,11 +12,6 @@
 #include "common.cuh"
 #include "internal.hpp"
 
-// 16-bit row kernels with packed FP32x2 arithmetic (1) or scalar FP32 (0)
-#ifndef JADE_ROWS_PACKED
-#define JADE_ROWS_PACKED 0
-#endif
-
 namespace jade {
 namespace {
 
@@ -122,33 +117,6 @@ __global__ void __launch_bounds__(kThreads) swiglu_bf16_kernel(const __nv_bfloat
         const uint64_t i = (nv << 3) + t;
         out[i] = __float2bfloat16_rn(swiglu1(__bfloat162float(g[i]), __bfloat162float(up[i])));
     }
-}
-
-// ------------------------------------------------------------------ packed FP32 pairs
-// sm_100 executes two FP32 operations per instruction on 64-bit register pairs
-// (fma/mul/add.rn.f32x2); the 16-bit row kernels use them to halve the
-// arithmetic instructions per element (their rows hold twice the elements per
-// byte of the FP32 ones).
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float &a, float &b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
 }
 
 // ------------------------------------------------------------------ block reductions
@@ -259,36 +227,11 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
         // its own maximum, so that its exponentials are e^-inf = 0, not e^(-inf + inf)
         const float shift = m == -INFINITY ? 0.0f : m;
         float s = 0.0f;
-#if JADE_ROWS_PACKED
-        if constexpr (sizeof(T) == 2) {
-            // 16-bit rows: (x - shift) * log2 e as one packed FMA per pair (relative
-            // error ~1e-6, far below the 16-bit output rounding), sums in pairs
-            const float l2e = 1.4426950408889634f;
-            const uint64_t k2 = f2_pack(l2e, l2e), c2 = f2_pack(-shift * l2e, -shift * l2e);
-            uint64_t s2 = f2_pack(0.0f, 0.0f);
-#pragma unroll
-            for (int j = 0; j < NV; ++j)
-                if (threadIdx.x + j * THREADS < nvec)
-#pragma unroll
-                    for (int e = 0; e < N; e += 2) {
-                        float a, b;
-                        f2_unpack(f2_fma(f2_pack(v[j][e], v[j][e + 1]), k2, c2), a, b);
-                        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v[j][e]) : "f"(a));
-                        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v[j][e + 1]) : "f"(b));
-                        s2 = f2_add(s2, f2_pack(v[j][e], v[j][e + 1]));
-                    }
-            float s0, s1;
-            f2_unpack(s2, s0, s1);
-            s = s0 + s1;
-        } else
-#endif
-        {
 #pragma unroll
         for (int j = 0; j < NV; ++j)
             if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
                 for (int e = 0; e < N; ++e) { v[j][e] = exp_neg(v[j][e] - shift); s += v[j][e]; }
-        }
         float mr = m, sr = s;
         block_reduce_softmax(mr, sr, scratch);
         const float inv = m == -INFINITY ? 0.0f : exp_neg(m - mr) / sr;  // a thread without elements stores nothing
@@ -297,45 +240,18 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
         for (int j = 0; j < NV; ++j) {
             const uint32_t c = threadIdx.x + j * THREADS;
             if (c < nvec) {
-#if JADE_ROWS_PACKED
-                if constexpr (sizeof(T) == 2) {
-                    const uint64_t inv2 = f2_pack(inv, inv);
-#pragma unroll
-                    for (int e = 0; e < N; e += 2) f2_unpack(f2_mul(f2_pack(v[j][e], v[j][e + 1]), inv2), v[j][e], v[j][e + 1]);
-                } else
-#endif
-                {
 #pragma unroll
                 for (int e = 0; e < N; ++e) v[j][e] *= inv;
-                }
                 Vec<T>::store(o + (uint64_t)c * N, v[j]);
             }
         }
     } else {
         float ss = 0.0f;
-#if JADE_ROWS_PACKED
-        if constexpr (sizeof(T) == 2) {  // two running sums of squares in one register pair
-            uint64_t ss2 = f2_pack(0.0f, 0.0f);
-#pragma unroll
-            for (int j = 0; j < NV; ++j)
-                if (threadIdx.x + j * THREADS < nvec)
-#pragma unroll
-                    for (int e = 0; e < N; e += 2) {
-                        const uint64_t x2 = f2_pack(v[j][e], v[j][e + 1]);
-                        ss2 = f2_fma(x2, x2, ss2);
-                    }
-            float s0, s1;
-            f2_unpack(ss2, s0, s1);
-            ss = s0 + s1;
-        } else
-#endif
-        {
 #pragma unroll
         for (int j = 0; j < NV; ++j)
             if (threadIdx.x + j * THREADS < nvec)
 #pragma unroll
                 for (int e = 0; e < N; ++e) ss = fmaf(v[j][e], v[j][e], ss);
-        }
         ss = block_reduce<false>(ss, scratch);
         const float inv = 1.0f / sqrtf(ss / (float)cols + eps);
         if constexpr (OP == RowOp::RmsInv) {
@@ -348,18 +264,8 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
                 if (c < nvec) {
                     float wv[N];
                     Vec<T>::load_keep(w + (uint64_t)c * N, wv);
-#if JADE_ROWS_PACKED
-                    if constexpr (sizeof(T) == 2) {  // (x * inv) * w, two elements per instruction
-                        const uint64_t inv2 = f2_pack(inv, inv);
-#pragma unroll
-                        for (int e = 0; e < N; e += 2)
-                            f2_unpack(f2_mul(f2_mul(f2_pack(v[j][e], v[j][e + 1]), inv2), f2_pack(wv[e], wv[e + 1])), v[j][e], v[j][e + 1]);
-                    } else
-#endif
-                    {
 #pragma unroll
                     for (int e = 0; e < N; ++e) v[j][e] = v[j][e] * inv * wv[e];
-                    }
                     Vec<T>::store(o + (uint64_t)c * N, v[j]);
                 }
             }
