@@ -18,9 +18,10 @@
 // word 8*phase + q holds rank q's latest arrival number for that phase, word
 // 16 + phase this rank's own count of its signals of that phase. A rank's k-th
 // signal of a phase carries the number k, and a waiter expects its own count,
-// so the flags never need resetting; all ranks launch the same sequence. Every
-// wait is bounded: on expiry it records kErrWaitPeer in the context's error word
-// (JR_ETIMEOUT) and the kernel returns.
+// so the flags never need resetting; all ranks launch the same sequence. Waits
+// run in a one-thread kernel ahead of the kernels that read the peers' data and
+// are bounded: on expiry they record kErrWaitPeer in the context's error word
+// (JR_ETIMEOUT) and return.
 //
 // Buffer reuse is ordered by the phases themselves: rank q's next scatter into
 // rank r's receive buffer comes after q's shard_gather, which waited for r's
@@ -60,26 +61,33 @@ __global__ void peer_signal_kernel(PeerSet flags, uint32_t ranks, uint32_t rank,
     for (uint32_t q = 0; q < ranks; ++q) st_release_sys(static_cast<uint32_t *>(flags.p[q]) + 8 * phase + rank, e);
 }
 
-// Thread 0 waits (bounded) until every rank's arrival number of `phase` reaches
-// this rank's own count; the block learns the outcome through shared memory.
-__device__ bool wait_arrivals(const uint32_t *local, uint32_t ranks, int phase, int *err) {
-    __shared__ int ok;
-    if (threadIdx.x == 0) {
-        const uint32_t e = *reinterpret_cast<const volatile uint32_t *>(local + 16 + phase);
-        ok = 1;
-        const uint64_t t0 = globaltimer();
-        for (uint32_t q = 0; q < ranks && ok; ++q)
-            while ((int)(ld_acquire_sys(local + 8 * phase + q) - e) < 0)
-                if (globaltimer() - t0 > kPeerWaitNs) {
-                    if (err) atomicCAS(err, 0, kErrWaitPeer);
-                    ok = 0;
-                    break;
-                }
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread of one block waits (bounded) until every rank's arrival number of
+// `phase` reaches this rank's own count: it polls with relaxed loads and a short
+// sleep (many pollers hammering one L2 line slowed the peers' stores landing in
+// this GPU's memory), then takes each arrival with an acquire load. The kernels
+// after it on the stream read the peers' data.
+__global__ void shard_wait_kernel(PeerSet flags, uint32_t ranks, uint32_t rank, int phase, int *err) {
+    if (threadIdx.x != 0) return;
+    const uint32_t *local = static_cast<const uint32_t *>(flags.p[rank]);
+    const uint32_t e = *reinterpret_cast<const volatile uint32_t *>(local + 16 + phase);
+    const uint64_t t0 = globaltimer();
+    for (uint32_t q = 0; q < ranks; ++q) {
+        while ((int)(ld_relaxed_sys(local + 8 * phase + q) - e) < 0) {
+            if (globaltimer() - t0 > kPeerWaitNs) {
+                if (err) atomicCAS(err, 0, kErrWaitPeer);
+                return;
+            }
+            __nanosleep(64);
+        }
+        (void)ld_acquire_sys(local + 8 * phase + q);
     }
-    __syncthreads();
-    const bool r = ok != 0;
-    __threadfence();
-    return r;
+    __threadfence_system();
 }
 
 __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 u) {
@@ -95,9 +103,7 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 u) {
 // This rank's rows: sum of the ranks' partial slots (rank order) plus the
 // residual, one BF16 rounding, stored into every rank's output.
 __global__ void __launch_bounds__(256) shard_reduce_kernel(const __nv_bfloat16 *__restrict__ recv, const __nv_bfloat16 *__restrict__ residual,
-                                                           PeerSet outs, PeerSet flags, uint32_t ranks, uint32_t rank, uint32_t rows_per,
-                                                           uint32_t cols, int *err) {
-    if (!wait_arrivals(static_cast<const uint32_t *>(flags.p[rank]), ranks, 0, err)) return;
+                                                           PeerSet outs, uint32_t ranks, uint32_t rank, uint32_t rows_per, uint32_t cols) {
     const uint64_t slot = (uint64_t)rows_per * cols;  // elements of one rank's partial rows
     const uint64_t nvec = slot / 8, own = (uint64_t)rank * slot;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -115,10 +121,6 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const __nv_bfloat16 *
             reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(outs.p[q]) + own)[v] = o;
         }
     }
-}
-
-__global__ void shard_wait_kernel(PeerSet flags, uint32_t ranks, uint32_t rank, int *err) {
-    wait_arrivals(static_cast<const uint32_t *>(flags.p[rank]), ranks, 1, err);
 }
 
 }  // namespace
@@ -149,7 +151,7 @@ LaunchFn make_shard_op(Context *ctx, const Spec &s, std::string &impl) {
         return [=](cudaStream_t st, void **b) {
             PeerSet flags{};
             if (!find_peers(ctx, b[1], ranks, flags)) return cudaErrorInvalidResourceHandle;
-            shard_wait_kernel<<<1, 32, 0, st>>>(flags, ranks, rank, err);
+            shard_wait_kernel<<<1, 32, 0, st>>>(flags, ranks, rank, 1, err);
             return cudaGetLastError();
         };
     }
@@ -162,9 +164,10 @@ LaunchFn make_shard_op(Context *ctx, const Spec &s, std::string &impl) {
         PeerSet outs{}, flags{};
         if (!find_peers(ctx, b[out_idx], ranks, outs) || !find_peers(ctx, b[out_idx + 1], ranks, flags))
             return cudaErrorInvalidResourceHandle;
+        // every rank's partial rows have arrived (phase 0), then the reduction
+        shard_wait_kernel<<<1, 32, 0, st>>>(flags, ranks, rank, 0, err);
         shard_reduce_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(b[0]),
-                                                  res ? static_cast<const __nv_bfloat16 *>(b[1]) : nullptr, outs, flags, ranks, rank,
-                                                  rows_per, cols, err);
+                                                  res ? static_cast<const __nv_bfloat16 *>(b[1]) : nullptr, outs, ranks, rank, rows_per, cols);
         const cudaError_t e = cudaGetLastError();
         return e != cudaSuccess ? e : launch_peer_signal(st, flags, ranks, rank, 1);
     };
