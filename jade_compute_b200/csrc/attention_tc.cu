@@ -34,8 +34,6 @@
 #include <cuda.h>
 
 #include <climits>
-#include <cstdlib>
-#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -109,7 +107,7 @@ struct WorkItems {
     }
 };
 
-template <int D, typename TIn, typename TOut, bool kDirectO>
+template <int D, typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, const AttnArgs args) {
@@ -118,9 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kIdescS = idesc_f32acc(kFmt, kFmt, false, false, kBQ, kBK);
     constexpr uint32_t kIdescO = idesc_f32acc(kFmt, kFmt, false, true, kBQ, D);
     constexpr int kDChunks = D / 64;
-    // 16-bit O leaves through TMA stores from a staging buffer, or (kDirectO) as
-    // 16-byte row stores straight from each softmax thread's registers
-    constexpr bool kStaged = !std::is_same<TOut, float>::value && !kDirectO;
+    constexpr bool kStaged = !std::is_same<TOut, float>::value;  // 16-bit O leaves through TMA stores
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -391,23 +387,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float inv = 1.0f / l_run;
             if constexpr (!kStaged) {
                 if (q < args.seq) {
-                    if constexpr (std::is_same<TOut, float>::value) {
-                        float *o = static_cast<float *>(args.out) + ((size_t)bh * args.seq + q) * D;
+                    float *o = static_cast<float *>(args.out) + ((size_t)bh * args.seq + q) * D;
 #pragma unroll
-                        for (int e = 0; e < D; e += 4)
-                            *reinterpret_cast<float4 *>(o + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
-                    } else {  // no staging buffer to wait for: the stores drain while the next item starts
-                        TOut *o = static_cast<TOut *>(args.out) + ((size_t)bh * args.seq + q) * D;
-#pragma unroll
-                        for (int oc = 0; oc < D; oc += 8) {
-                            uint4 u;
-                            u.x = pack16<kFmt>(r[oc] * inv, r[oc + 1] * inv);
-                            u.y = pack16<kFmt>(r[oc + 2] * inv, r[oc + 3] * inv);
-                            u.z = pack16<kFmt>(r[oc + 4] * inv, r[oc + 5] * inv);
-                            u.w = pack16<kFmt>(r[oc + 6] * inv, r[oc + 7] * inv);
-                            *reinterpret_cast<uint4 *>(o + oc) = u;
-                        }
-                    }
+                    for (int e = 0; e < D; e += 4)
+                        *reinterpret_cast<float4 *>(o + e) = make_float4(r[e] * inv, r[e + 1] * inv, r[e + 2] * inv, r[e + 3] * inv);
                 }
             } else {
                 // stage O in the Q tensor map's layout (64-column chunks, 128-byte
@@ -481,20 +464,10 @@ bool make_map3(CUtensorMap *map, CUtensorMapDataType dt, const void *ptr, uint64
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// How 16-bit O leaves the two-tile kernel: JADE_ATTENTION_O_STORE=direct (row
-// stores from registers) or tma (staging buffer and TMA stores, the default);
-// read when a kernel is compiled.
-bool attention_direct_o() {
-    const char *v = std::getenv("JADE_ATTENTION_O_STORE");
-    if (!v || !*v || !std::strcmp(v, "tma")) return false;
-    if (!std::strcmp(v, "direct")) return true;
-    throw IrError("JADE_ATTENTION_O_STORE must be direct or tma");
-}
-
-template <int D, typename TIn, typename TOut, bool kDirectO>
+template <int D, typename TIn, typename TOut>
 LaunchFn attn_launch(Context *ctx, const Spec &s) {
     using L = AttnLayout<D>;
-    auto kernel = attention_tc_kernel<D, TIn, TOut, kDirectO>;
+    auto kernel = attention_tc_kernel<D, TIn, TOut>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem) != cudaSuccess)
         throw IrError("cannot reserve shared memory for the tcgen05 attention");
 
@@ -541,20 +514,12 @@ LaunchFn make_attention_tc(Context *ctx, const Spec &s, std::string &impl) {
     impl = std::string("attention_tcgen05_fa_2xq128_kv128_d") + std::to_string(s.dim) + "_" + dtype_name(s.dtype) + "_out_" +
            dtype_name(s.out_dtype) + (s.causal ? "_causal" : "");
     const bool f32out = s.out_dtype == DType::F32;
-    if (f32out) {
-        if (s.dtype == DType::BF16) return s.dim == 128 ? attn_launch<128, __nv_bfloat16, float, false>(ctx, s)
-                                                        : attn_launch<64, __nv_bfloat16, float, false>(ctx, s);
-        return s.dim == 128 ? attn_launch<128, __half, float, false>(ctx, s) : attn_launch<64, __half, float, false>(ctx, s);
-    }
-    const bool direct = attention_direct_o();
-    if (direct) impl += "_direct_o";
     if (s.dtype == DType::BF16) {
-        if (s.dim == 128) return direct ? attn_launch<128, __nv_bfloat16, __nv_bfloat16, true>(ctx, s)
-                                        : attn_launch<128, __nv_bfloat16, __nv_bfloat16, false>(ctx, s);
-        return direct ? attn_launch<64, __nv_bfloat16, __nv_bfloat16, true>(ctx, s) : attn_launch<64, __nv_bfloat16, __nv_bfloat16, false>(ctx, s);
+        if (s.dim == 128) return f32out ? attn_launch<128, __nv_bfloat16, float>(ctx, s) : attn_launch<128, __nv_bfloat16, __nv_bfloat16>(ctx, s);
+        return f32out ? attn_launch<64, __nv_bfloat16, float>(ctx, s) : attn_launch<64, __nv_bfloat16, __nv_bfloat16>(ctx, s);
     }
-    if (s.dim == 128) return direct ? attn_launch<128, __half, __half, true>(ctx, s) : attn_launch<128, __half, __half, false>(ctx, s);
-    return direct ? attn_launch<64, __half, __half, true>(ctx, s) : attn_launch<64, __half, __half, false>(ctx, s);
+    if (s.dim == 128) return f32out ? attn_launch<128, __half, float>(ctx, s) : attn_launch<128, __half, __half>(ctx, s);
+    return f32out ? attn_launch<64, __half, float>(ctx, s) : attn_launch<64, __half, __half>(ctx, s);
 }
 
 }  // namespace jade
