@@ -41,10 +41,9 @@ struct Context {
     // cuBLAS handle for the gemm_mps library comparator (lazy)
     void *cublas = nullptr;
     // peer memory (jr_peer_attach): a local buffer -> every rank's device address
-    // of its counterpart (this rank's own entry is the buffer itself), and the
-    // mappings this context opened
+    // of its counterpart (this rank's own entry is the buffer itself; the others
+    // are CUDA IPC mappings this context opened and closes with the buffer)
     std::map<uintptr_t, std::vector<void *>> peers;
-    std::vector<void *> ipc_opened;
     // runtime-compiled elementwise modules, keyed by full source text
     std::map<std::string, std::pair<void *, void *>> rtc_modules;  // source -> (CUmodule, CUfunction)
     std::mutex rtc_mutex;
@@ -114,6 +113,7 @@ cudaError_t launch_peer_signal(cudaStream_t st, const PeerSet &flags, uint32_t r
 void cublas_destroy(Context *ctx);
 void rtc_destroy(Context *ctx);
 void comm_destroy(Context *ctx);
+void peer_detach(Context *ctx, const void *local);  // closes the mappings of one attached buffer
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
 void *driver_entry(const char *name);

@@ -138,6 +138,14 @@ PeerSet peer_set(Context *ctx, const void *local, uint32_t ranks) {
     return s;
 }
 
+void peer_detach(Context *ctx, const void *local) {
+    const auto it = ctx->peers.find(reinterpret_cast<uintptr_t>(local));
+    if (it == ctx->peers.end()) return;
+    for (void *p : it->second)
+        if (p && p != local) cudaIpcCloseMemHandle(p);
+    ctx->peers.erase(it);
+}
+
 cudaError_t launch_peer_signal(cudaStream_t st, const PeerSet &flags, uint32_t ranks, uint32_t rank, int phase) {
     peer_signal_kernel<<<1, 32, 0, st>>>(flags, ranks, rank, phase);
     return cudaGetLastError();
@@ -216,8 +224,6 @@ extern "C" int jr_peer_attach(void *handle, const void *ptr, const unsigned char
             }
             ptrs[q] = p;
         }
-        for (void *p : ptrs)
-            if (p != ptr) ctx->ipc_opened.push_back(p);
         ctx->peers[reinterpret_cast<uintptr_t>(ptr)] = std::move(ptrs);
     });
 }

@@ -66,9 +66,7 @@ void teardown(Context *ctx) {
     jade::comm_destroy(ctx);
     jade::cublas_destroy(ctx);
     jade::rtc_destroy(ctx);
-    for (void *p : ctx->ipc_opened) cudaIpcCloseMemHandle(p);
-    ctx->ipc_opened.clear();
-    ctx->peers.clear();
+    while (!ctx->peers.empty()) jade::peer_detach(ctx, reinterpret_cast<void *>(ctx->peers.begin()->first));
     for (const auto &entry : ctx->allocations) {
         void *p = reinterpret_cast<void *>(entry.first);
         if (entry.second.host) cudaFreeHost(p);
@@ -253,6 +251,7 @@ extern "C" void jr_free(void *handle, void *ptr) {
         if (it->second.host) return;  // pinned host buffers go through jr_host_free
         ctx->allocations.erase(it);
     }
+    jade::peer_detach(ctx, ptr);  // a later allocation at this address is not attached
     cudaFree(ptr);
 }
 

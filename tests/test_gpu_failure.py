@@ -57,3 +57,23 @@ def test_expiry_inside_a_batch_stops_the_batch_report():
         rt.execute([(fill, [x])])  # and the next batch succeeds
     finally:
         rt.close()
+
+
+def test_peer_attachment_ends_with_its_buffer():
+    # a freed buffer's peer mappings close with it: a new buffer (possibly at the
+    # same address) is not attached until it is shared again
+    from jade_compute_b200.parallel import share_buffers
+    rt = jc.Runtime(0)
+    try:
+        y, flags = rt.alloc(128 * 8, "bf16"), rt.alloc_bytes(256)
+        share_buffers(rt, None, [y, flags])
+        gather = rt.compile({"op": "shard_gather", "rows": 128, "cols": 8, "ranks": 1, "rank": 0, "dtype": "bf16"})
+        rt.execute([(gather, [y, flags])])
+        flags.free()
+        fresh = rt.alloc_bytes(256)
+        with pytest.raises(JadeError, match="not attached to peer memory"):
+            rt.execute([(gather, [y, fresh])])
+        share_buffers(rt, None, [fresh])
+        rt.execute([(gather, [y, fresh])])
+    finally:
+        rt.close()
