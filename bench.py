@@ -316,17 +316,18 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     rank = dist.get_rank() if dist is not None else 0
     if world > 1 and MLP_COMM[0] == "nccl":
         parallel.init_comm(rt, dist, timeout_ms=120000)
-    # tensor parallel: row blocks, each block's all-reduce on the collective stream
-    # beside the next block's GEMMs, whose grids leave SMs for NCCL. Smaller blocks
-    # cost GEMM wave efficiency, so they pay only where the all-reduce is a large
-    # share of the step (measured at 2 GPUs: one block is 9% faster than four)
+    # tensor parallel: optionally in row blocks (--mlp-chunks), each block's
+    # all-reduce on the collective stream beside the next block's GEMMs, whose grids
+    # leave SMs for NCCL. Smaller blocks cost GEMM wave efficiency: one block measured
+    # faster than four at 2 GPUs (7.0 vs 6.3 M tokens/s) and than two at 4 GPUs
+    # (11.1 vs 9.8), so the default is one block
     comm = MLP_COMM[0] if world > 1 else "nccl"
     if comm == "peer":
         # the down GEMM scatters its partial rows to their owners over NVLink,
         # owners reduce and push their rows to every rank (csrc/peer.cu)
         chunks, sm_limit = 1, 0
     else:
-        chunks = MLP_CHUNKS[0] if MLP_CHUNKS[0] > 0 else {1: 1, 2: 1, 4: 2}.get(world, 4)
+        chunks = MLP_CHUNKS[0] if MLP_CHUNKS[0] > 0 else 1
         sm_limit = MLP_SM_LIMIT[0] if chunks > 1 else 0
     mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit, comm=comm)
     if comm == "peer":
@@ -719,7 +720,7 @@ def _main(out_fd):
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--mlp-chunks", type=int, default=MLP_CHUNKS[0],
-                    help="row blocks of the tensor-parallel MLP (0: 1 up to 2 GPUs, 2 at 4, 4 at 8)")
+                    help="row blocks of the tensor-parallel MLP (0 = one block)")
     ap.add_argument("--mlp-comm", choices=["nccl", "peer"], default=MLP_COMM[0],
                     help="tensor-parallel MLP collective: NCCL all-reduce or NVLink peer scatter/reduce")
     ap.add_argument("--mlp-sm-limit", type=int, default=MLP_SM_LIMIT[0],

@@ -347,10 +347,20 @@ LaunchFn make_gemm_simt(Context *ctx, const Spec &s, std::string &impl) {
     const int sms = ctx->sm_count;
     const char *force = std::getenv("JADE_FFMA_TILE");
     if (ffma_tma_fits(s) && !(force && *force)) {
+        // the largest tile that still gives every SM a block (128x128: 8x8 outputs
+        // per thread), else 32x64 while that gives two blocks per SM, else 16x32
+        // blocks of one warp (512^3: 512 blocks, ~3.5 warps per SM instead of one)
         const long long big_tiles = (long long)((s.m + 127) / 128) * ((s.n + 127) / 128);
+        const long long mid_tiles = (long long)((s.m + 31) / 32) * ((s.n + 63) / 64);
         if (big_tiles >= sms) {
             impl += "_tma_128x128";
             return ffma_tma_launch<128, 128, 8, 8, 4>(ctx, s);
+        }
+        const char *small = std::getenv("JADE_FFMA_SMALL");  // 32x64 or 16x32: forces the small-shape tile
+        const bool tiny = small && *small ? std::strcmp(small, "16x32") == 0 : mid_tiles < 2LL * sms;
+        if (tiny) {
+            impl += "_tma_16x32";
+            return ffma_tma_launch<16, 32, 4, 4, 4>(ctx, s);
         }
         impl += "_tma_32x64";
         return ffma_tma_launch<32, 64, 4, 4, 4>(ctx, s);
