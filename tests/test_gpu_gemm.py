@@ -145,7 +145,7 @@ BIG = [("bf16", False, "fp32", 2048), ("bf16", True, "fp32", 2048), ("bf16", Fal
        ("bf16", True, "bf16", 2048), ("bf16", False, "fp32", 8192), ("bf16", False, "bf16", 8192),
        ("bf16", True, "fp32", 8192), ("bf16", True, "bf16", 8192), ("bf16", False, "fp32", 16384),
        ("tf32", False, "fp32", 2048), ("tf32", False, "fp32", 4096), ("tf32", True, "fp32", 4096),
-       ("tf32", False, "fp32", 8192)]
+       ("tf32", False, "fp32", 8192), ("fp16", False, "fp32", 8192), ("fp16", True, "fp16", 4096)]
 
 
 @pytest.mark.parametrize("dtype,b_nk,out_dtype,size", BIG, ids=lambda v: str(v))
@@ -161,7 +161,7 @@ def test_tc_gemm_baseline_sizes_sampled(rt, dtype, b_nk, out_dtype, size):
     if dtype == "tf32":
         coef = 0.0012
     else:
-        coef = 2 * k * 2.0 ** -23 + (2.0 ** -8 if out_dtype == "bf16" else 0.0)
+        coef = 2 * k * 2.0 ** -23 + {"bf16": 2.0 ** -8, "fp16": 2.0 ** -11}.get(out_dtype, 0.0)
     rc, v = O.validation_check(m, n, k, af, bf, got, budget=1 << 14, coef=coef)
     assert rc == 0, (rc, v.first_bad_index, v.max_scaled_error, kern.info["impl"])
     print(f"{kern.info['impl']} {size}^3: max |err|/sum|a*b| = {v.max_magnitude_error:.2e}, "
