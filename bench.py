@@ -350,6 +350,12 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
            "kernels": [k.info.get("impl") for k, _ in jobs], "clocks": clk.summary()}
     if world > 1:
+        # every rank's region and per-job times (the slowest rank sets ms_per_step)
+        import torch
+        mine = torch.tensor([t.gpu_ms / steps] + [x / steps for x in t.job_ms], dtype=torch.float64)
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        out["per_rank_ms"] = [[round(v, 4) for v in e.tolist()] for e in every]
         # time of the collective jobs per block (all row blocks), and for the NCCL
         # all-reduce its bus bandwidth: 2 (N-1)/N x bytes / time
         job_ms = [x / steps for x in t.job_ms]
