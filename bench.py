@@ -241,8 +241,9 @@ def gemm_bench(rt, dist, world, steps, warmup, peaks, device=0, m=8192):
     g = rt.compile({"op": "gemm", "m": m, "n": n, "k": m, "tiled": True, "dtype": "bf16", "out_dtype": "bf16",
                     "b_layout": layout})
     rt.execute([(g, [a, b, c])], repeats=max(warmup, 3))
+    clk = ClockSampler(device)  # NVML set-up before the barrier: ranks start the timed region together
     barrier(dist)
-    with ClockSampler(device) as clk:
+    with clk:
         t = rt.execute([(g, [a, b, c])], repeats=steps, per_job=True)
     ms = reduce_max(dist, t.job_ms[0] / steps)
     tflops = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
@@ -336,8 +337,9 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     jobs = mlp.jobs()
     lanes = chunks > 1
     rt.execute(jobs, repeats=max(warmup, 3), streams=lanes)
+    clk = ClockSampler(rt.device)  # NVML set-up before the barrier: ranks start the timed region together
     barrier(dist)
-    with ClockSampler(rt.device) as clk:
+    with clk:
         t = rt.execute(jobs, repeats=steps, per_job=True, streams=lanes)
     ms = reduce_max(dist, t.gpu_ms / steps)
     flops = 6.0 * T * d * ffn
@@ -389,9 +391,10 @@ def c5_attention(rt, dist, world, rank, steps, warmup, peaks, device=0, seqs=(40
             rt.fill(buf, "normal", seed=8, stream=i + 4 * rank, lo=0.0, hi=1.0)
         attn = rt.compile({"op": "attention_online", "heads": nh, "seq": seq, "dim": D, "causal": causal, "dtype": "bf16"})
         rt.execute([(attn, [q, k, v, o])], repeats=max(warmup, 2))
-        barrier(dist)
         reps = max(3, min(steps, 20))
-        with ClockSampler(device) as clk:
+        clk = ClockSampler(device)  # NVML set-up before the barrier: ranks start the timed region together
+        barrier(dist)
+        with clk:
             t = rt.execute([(attn, [q, k, v, o])], repeats=reps, per_job=True)
         ms = reduce_max(dist, t.job_ms[0] / reps)
         flops = causal_flops(Bs, Hs, seq, D) if causal else full_flops(Bs, Hs, seq, D)
@@ -421,8 +424,9 @@ def c5_gemms(rt, dist, world, rank, steps, warmup, peaks, device=0, sizes=(1024,
             g = rt.compile({"op": "gemm", "m": m, "n": n, "k": m, "tiled": True, "dtype": dtype, "b_layout": "nk"})
             reps = max(3, min(steps, int(2e13 / (2.0 * m ** 3)) + 1))
             rt.execute([(g, [a, b, c])], repeats=max(warmup, 2))
+            clk = ClockSampler(device)  # NVML set-up before the barrier: ranks start the timed region together
             barrier(dist)
-            with ClockSampler(device) as clk:
+            with clk:
                 t = rt.execute([(g, [a, b, c])], repeats=reps, per_job=True)
             ms = reduce_max(dist, t.job_ms[0] / reps)
             tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
@@ -606,8 +610,9 @@ def run_ours(args):
     try:
         jobs, attn, (q, k, v, o), flush_buf = attention_bench(rt, jc, args.steps, args.warmup, True, B)
         flops = causal_flops(B, H, S, D)
+        clk = ClockSampler(local)  # NVML set-up before the barrier: ranks start the timed region together
         barrier(dist)
-        with ClockSampler(local) as clk:
+        with clk:
             t = rt.execute(jobs, repeats=args.steps, per_job=True)
         attn_ms_total = t.job_ms[1]
         region_ms = t.gpu_ms
