@@ -315,7 +315,9 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     from jade_compute_b200.mlp import ResidualMLP
     T, d, ffn = 8192, 4096, 14336
     rank = dist.get_rank() if dist is not None else 0
-    if world > 1 and MLP_COMM[0] == "nccl":
+    if world > 1:
+        # NCCL carries the all-reduce in "nccl" mode and, in both modes, the start
+        # gate of the timed region below
         parallel.init_comm(rt, dist, timeout_ms=120000)
     # tensor parallel: optionally in row blocks (--mlp-chunks), each block's
     # all-reduce on the collective stream beside the next block's GEMMs, whose grids
@@ -338,15 +340,33 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     lanes = chunks > 1
     rt.execute(jobs, repeats=max(warmup, 3), streams=lanes)
     clk = ClockSampler(rt.device)  # NVML set-up before the barrier: ranks start the timed region together
+    gate = None
+    if world > 1 and not lanes:
+        # the ranks' steps are coupled through the collective, so a rank whose host
+        # leaves the CPU barrier first would count the others' lateness (milliseconds
+        # of host skew) as its own step time. A one-element NCCL all-reduce ahead of
+        # the steps releases every GPU within microseconds; its own time is measured
+        # and left out of the region
+        gate_buf = rt.alloc(64, "fp32")
+        gate = rt.compile({"op": "all_reduce", "len": 64, "dtype": "fp32"})
+        rt.execute([(gate, [gate_buf])])
     barrier(dist)
     with clk:
-        t = rt.execute(jobs, repeats=steps, per_job=True, streams=lanes)
-    ms = reduce_max(dist, t.gpu_ms / steps)
+        if gate is not None:
+            t = rt.execute([(gate, [gate_buf])] + jobs * steps, per_job=True)
+            gate_ms = t.job_ms[0]
+            region = t.gpu_ms - gate_ms
+            job_ms = [sum(t.job_ms[1 + i::len(jobs)]) for i in range(len(jobs))]
+        else:
+            t = rt.execute(jobs, repeats=steps, per_job=True, streams=lanes)
+            region, job_ms, gate_ms = t.gpu_ms, t.job_ms, None
+    job_ms = [x / steps for x in job_ms]
+    ms = reduce_max(dist, region / steps)
     flops = 6.0 * T * d * ffn
     per_gpu_tflops = flops / world / (ms * 1e-3) / 1e12
     out = {"workload": f"residual MLP block T={T} d={d} ffn={ffn} BF16 (BASELINE configs[3]), tensor parallel x{world}",
            "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
-           "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": [x / steps for x in t.job_ms],
+           "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": job_ms,
            "row_blocks": chunks, "gemm_sm_limit": sm_limit or None, "collective": comm if world > 1 else None,
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
@@ -354,13 +374,13 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     if world > 1:
         # every rank's region and per-job times (the slowest rank sets ms_per_step)
         import torch
-        mine = torch.tensor([t.gpu_ms / steps] + [x / steps for x in t.job_ms], dtype=torch.float64)
+        mine = torch.tensor([region / steps] + job_ms, dtype=torch.float64)
         every = [torch.zeros_like(mine) for _ in range(world)]
         dist.all_gather(every, mine)
         out["per_rank_ms"] = [[round(v, 4) for v in e.tolist()] for e in every]
+        out["start_gate_ms"] = gate_ms
         # time of the collective jobs per block (all row blocks), and for the NCCL
         # all-reduce its bus bandwidth: 2 (N-1)/N x bytes / time
-        job_ms = [x / steps for x in t.job_ms]
         if comm == "nccl":
             coll_ms = sum(ms_ for (k, _), ms_ in zip(jobs, job_ms) if k is mlp.k_ar)
             out["collective_ms"] = coll_ms
@@ -369,7 +389,10 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
             out["collective_ms"] = sum(ms_ for (k, _), ms_ in zip(jobs, job_ms) if k in (mlp.k_reduce, mlp.k_gather))
     if check:
         out["max_err"] = mlp_error(rt, mlp, world, seed=11)
-    if world > 1 and comm == "nccl":
+    if gate is not None:
+        gate.release()
+        gate_buf.free()
+    if world > 1:
         rt.comm_destroy()
     return out
 

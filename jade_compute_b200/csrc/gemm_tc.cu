@@ -54,6 +54,10 @@ struct GemmArgs {
     // [r * rows_per_rank, (r + 1) * rows_per_rank), this GEMM's rank is my_rank
     void *scatter[kMaxPeerRanks];
     int rows_per_rank, my_rank;
+    // M-blocks the raster is rotated by: the scatter GEMM starts with the next
+    // rank's rows and ends with its own, so the tiles computed last are written to
+    // local memory and no NVLink transfer trails the last MMA
+    int m_rotate;
 };
 
 // M-blocks per raster group: as many as keep the group's A rows (group x 128 x K
@@ -70,13 +74,14 @@ int raster_group(int tiles_m, uint64_t k, int eb) {
 // of a group before the next group, M fastest inside a group. A group's A rows
 // stay in L2 while its N-blocks stream past, so B is read from DRAM about
 // tiles_m / group times and A about once.
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int &tm, int &tn) {
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int rotate, int &tm, int &tn) {
     const int per_group = group * tiles_n;
     const int g = t / per_group, first_m = g * group;
     const int gm = min(tiles_m - first_m, group);
     const int r = t % per_group;
     tm = first_m + r % gm;
     tn = r / gm;
+    if (rotate) tm = (tm + rotate) % tiles_m;
 }
 
 template <typename TOut>
@@ -244,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t last_phase[kStages] = {};
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
                 int tm, tn;
-                tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+                tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, args.m_rotate, tm, tn);
                 const int m0 = tm * BM, nb0 = tn * BN;  // B rows (nk) or columns (kn) of this tile
                 for (int kb = 0; kb < args.kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
@@ -312,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ResidualChunk<TOut> res_next;
         for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
             int tm, tn;
-            tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, tm, tn);
+            tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, args.m_rotate, tm, tn);
             if constexpr (kEpi == kEpiResidual)  // the residual does not wait for the MMAs: fetch chunk 0 now
                 load_residual(res_next, static_cast<const TOut *>(args.residual), tm * BM + quarter * 32, r_sub, tn * BN + c_sub,
                               args.M, args.N, (args.N % 4) == 0);
@@ -450,6 +455,7 @@ LaunchFn tc_launch(Context *ctx, const Spec &s) {
     if (kEpi == kEpiScatter) {
         base.rows_per_rank = (int)(s.m / s.ranks);
         base.my_rank = (int)s.rank;
+        base.m_rotate = (int)(((s.rank + 1) % s.ranks) * (s.m / s.ranks) / BM);
     }
     const uint64_t M = s.m, K = s.k;
     return [=](cudaStream_t st, void **b) {

@@ -8,6 +8,8 @@
 // from HBM exactly once (the reference reads it 2-3 times).
 #include <algorithm>
 #include <cfloat>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "internal.hpp"
@@ -179,6 +181,10 @@ template <> struct Vec<float> {
         const float4 v = *reinterpret_cast<const float4 *>(p);
         d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
     }
+    __device__ static void unpack(uint4 v, float *d) {
+        d[0] = __uint_as_float(v.x); d[1] = __uint_as_float(v.y); d[2] = __uint_as_float(v.z); d[3] = __uint_as_float(v.w);
+    }
+    __device__ static void store_shared(float *p, const float *d) { *reinterpret_cast<float4 *>(p) = make_float4(d[0], d[1], d[2], d[3]); }
     __device__ static void store(float *p, const float *d) {
         __stcs(reinterpret_cast<float4 *>(p), make_float4(d[0], d[1], d[2], d[3]));
     }
@@ -193,13 +199,15 @@ template <> struct Vec<__nv_bfloat16> {
     __device__ static void load(const __nv_bfloat16 *p, float *d) { unpack(__ldcs(reinterpret_cast<const uint4 *>(p)), d); }
     __device__ static void load_keep(const __nv_bfloat16 *p, float *d) { unpack(__ldg(reinterpret_cast<const uint4 *>(p)), d); }
     __device__ static void load_shared(const __nv_bfloat16 *p, float *d) { unpack(*reinterpret_cast<const uint4 *>(p), d); }
-    __device__ static void store(__nv_bfloat16 *p, const float *d) {
+    __device__ static uint4 pack(const float *d) {
         uint4 v;
         uint32_t *a = reinterpret_cast<uint32_t *>(&v);
 #pragma unroll
         for (int q = 0; q < 4; ++q) a[q] = pack_bf16(d[2 * q], d[2 * q + 1]);
-        __stcs(reinterpret_cast<uint4 *>(p), v);
+        return v;
     }
+    __device__ static void store(__nv_bfloat16 *p, const float *d) { __stcs(reinterpret_cast<uint4 *>(p), pack(d)); }
+    __device__ static void store_shared(__nv_bfloat16 *p, const float *d) { *reinterpret_cast<uint4 *>(p) = pack(d); }
 };
 
 // Row kernels, register-resident: one block per row (grid-stride over rows),
@@ -212,10 +220,19 @@ enum class RowOp { RmsNorm, Softmax, RmsInv };
 // rounding than exp(x - row max) / sum, for one block reduction instead of two;
 // exponentials on the MUFU unit, exp_neg);
 // RMSNorm = sum of squares, scale by inv*w; RmsInv = the per-row inverse RMS only.
-template <typename T, int NV, RowOp OP, int THREADS>
+// SINK: results go to `sink` (the row's shared-memory stage, written back by bulk
+// copies) instead of global memory; WPRE: the RMSNorm weights come from `wpre`, the
+// thread's weight vectors held in registers across rows (the columns of a thread
+// are the same in every row).
+template <typename T, int NV, RowOp OP, int THREADS, bool SINK = false, bool WPRE = false>
 __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t row, uint32_t nvec, uint32_t cols, const T *__restrict__ w,
-                                            void *__restrict__ out_, float eps, float *scratch) {
+                                            void *__restrict__ out_, float eps, float *scratch, T *sink = nullptr,
+                                            const uint4 *wpre = nullptr) {
     constexpr int N = Vec<T>::N;
+    auto put = [&](uint32_t c, const float *d) {
+        if constexpr (SINK) Vec<T>::store_shared(sink + (uint64_t)c * N, d);
+        else Vec<T>::store(static_cast<T *>(out_) + (uint64_t)row * cols + (uint64_t)c * N, d);
+    };
     if constexpr (OP == RowOp::Softmax) {
         float m = -INFINITY;
 #pragma unroll
@@ -235,14 +252,13 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
         float mr = m, sr = s;
         block_reduce_softmax(mr, sr, scratch);
         const float inv = m == -INFINITY ? 0.0f : exp_neg(m - mr) / sr;  // a thread without elements stores nothing
-        T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const uint32_t c = threadIdx.x + j * THREADS;
             if (c < nvec) {
 #pragma unroll
                 for (int e = 0; e < N; ++e) v[j][e] *= inv;
-                Vec<T>::store(o + (uint64_t)c * N, v[j]);
+                put(c, v[j]);
             }
         }
     } else {
@@ -257,16 +273,16 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
         if constexpr (OP == RowOp::RmsInv) {
             if (threadIdx.x == 0) static_cast<float *>(out_)[row] = inv;
         } else {
-            T *o = static_cast<T *>(out_) + (uint64_t)row * cols;
 #pragma unroll
             for (int j = 0; j < NV; ++j) {
                 const uint32_t c = threadIdx.x + j * THREADS;
                 if (c < nvec) {
                     float wv[N];
-                    Vec<T>::load_keep(w + (uint64_t)c * N, wv);
+                    if constexpr (WPRE) Vec<T>::unpack(wpre[j], wv);
+                    else Vec<T>::load_keep(w + (uint64_t)c * N, wv);
 #pragma unroll
                     for (int e = 0; e < N; ++e) v[j][e] = v[j][e] * inv * wv[e];
-                    Vec<T>::store(o + (uint64_t)c * N, v[j]);
+                    put(c, v[j]);
                 }
             }
         }
@@ -292,26 +308,42 @@ __global__ void __launch_bounds__(THREADS) row_kernel(const T *__restrict__ x, c
 }
 
 // Row kernels with the rows staged in shared memory: thread 0 streams whole rows
-// (bulk copies counted on an mbarrier) into a ring of kRowStages buffers, running
-// kRowStages - 1 rows ahead of the arithmetic, so each SM keeps ~100 KB of reads in
+// (bulk copies counted on an mbarrier) into a ring of STAGES buffers, running up
+// to STAGES rows ahead of the arithmetic, so each SM keeps ~100 KB of reads in
 // flight through the reductions and stores of the current row (the register
 // kernel has reads in flight only between its row loads and first reduction).
 // Persistent: as many CTAs as fit, rows dealt round-robin.
-constexpr int kRowStages = 3;
+//
+// BULK: the results are written back into the row's own stage and leave by bulk
+// copies (one thread issues them; the copy engine writes whole lines), instead of
+// 16-byte stores from every thread. A stage is then refilled one iteration later,
+// once its store has read it out, so STAGES - 1 rows are in flight ahead of the
+// arithmetic. RMSNorm rows of up to 4 vectors per thread keep the thread's weights
+// in registers for all rows.
 constexpr uint32_t kRowChunk = 8192;  // bytes per bulk copy
 
-template <typename T, int NV, RowOp OP>
+template <typename T, int NV, RowOp OP, int STAGES, bool BULK>
 __global__ void __launch_bounds__(kThreads) row_staged_kernel(const T *__restrict__ x, const T *__restrict__ w, void *__restrict__ out_,
                                                               uint32_t rows, uint32_t cols, float eps, uint32_t stage_bytes, int *err) {
     extern __shared__ __align__(128) uint8_t stage[];
     __shared__ float scratch[64];
-    __shared__ uint64_t full[kRowStages];
+    __shared__ uint64_t full[STAGES];
     __shared__ int abort_flag;
     constexpr int N = Vec<T>::N;
+    constexpr bool kWpre = false;
+    static_assert(!BULK || OP != RowOp::RmsInv, "RmsInv writes one value per row");
     const uint32_t nvec = cols / N, row_bytes = cols * (uint32_t)sizeof(T);
-    int issued[kRowStages] = {};  // thread 0: rows loaded into each stage
+    uint4 wpre[kWpre ? NV : 1];
+    if constexpr (kWpre) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const uint32_t c = threadIdx.x + j * kThreads;
+            if (c < nvec) wpre[j] = __ldg(reinterpret_cast<const uint4 *>(w + (uint64_t)c * N));
+        }
+    }
+    int issued[STAGES] = {};  // thread 0: rows loaded into each stage
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kRowStages; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
         abort_flag = 0;
         fence_barrier_init();
     }
@@ -324,33 +356,57 @@ __global__ void __launch_bounds__(kThreads) row_staged_kernel(const T *__restric
         ++issued[s];
     };
     if (threadIdx.x == 0)
-        for (int s = 0; s < kRowStages; ++s) {
+        for (int s = 0; s < STAGES; ++s) {
             const uint64_t row = blockIdx.x + (uint64_t)s * gridDim.x;
             if (row < rows) issue((uint32_t)row, s);
         }
     uint32_t k = 0;
     for (uint32_t row = blockIdx.x; row < rows; row += gridDim.x, ++k) {
-        const int s = k % kRowStages;
+        const int s = k % STAGES;
         bool ok = true;
-        if (threadIdx.x == 0) ok = mbar_wait(&full[s], (k / kRowStages) & 1, &abort_flag, err, kErrWaitTmaFull);
+        if (threadIdx.x == 0) ok = mbar_wait(&full[s], (k / STAGES) & 1, &abort_flag, err, kErrWaitTmaFull);
         if (__syncthreads_or(!ok)) break;  // a uniform exit; also publishes the staged row to every thread
-        const T *xr = reinterpret_cast<const T *>(stage + s * stage_bytes);
+        T *xr = reinterpret_cast<T *>(stage + s * stage_bytes);
         float v[NV][N];
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
             const uint32_t c = threadIdx.x + j * kThreads;
             if (c < nvec) Vec<T>::load_shared(xr + (uint64_t)c * N, v[j]);
         }
-        __syncthreads();  // the stage is read out: it takes the row kRowStages ahead
-        if (threadIdx.x == 0) {
-            const uint64_t next = row + (uint64_t)kRowStages * gridDim.x;
-            if (next < rows) issue((uint32_t)next, s);
+        if constexpr (!BULK) {
+            __syncthreads();  // the stage is read out: it takes the row STAGES ahead
+            if (threadIdx.x == 0) {
+                const uint64_t next = row + (uint64_t)STAGES * gridDim.x;
+                if (next < rows) issue((uint32_t)next, s);
+            }
+            row_compute<T, NV, OP, kThreads, false, kWpre>(v, row, nvec, cols, w, out_, eps, scratch, nullptr, wpre);
+        } else {
+            // every thread overwrites only the vectors it read, so no barrier is
+            // needed between the loads above and these stores
+            row_compute<T, NV, OP, kThreads, true, kWpre>(v, row, nvec, cols, w, out_, eps, scratch, xr, wpre);
+            fence_proxy_async();  // this thread's shared stores, visible to the bulk copies
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                uint8_t *dst = reinterpret_cast<uint8_t *>(static_cast<T *>(out_) + (uint64_t)row * cols);
+                for (uint32_t o = 0; o < row_bytes; o += kRowChunk)
+                    bulk_store(dst + o, reinterpret_cast<uint8_t *>(xr) + o, min(kRowChunk, row_bytes - o));
+                bulk_commit_group();
+                if (k > 0) {  // the previous iteration's stage, once its store has read it out
+                    const uint64_t next = row + (uint64_t)(STAGES - 1) * gridDim.x;
+                    if (next < rows) {
+                        bulk_wait_read_but_one();
+                        issue((uint32_t)next, (k - 1) % STAGES);
+                    }
+                }
+            }
         }
-        row_compute<T, NV, OP, kThreads>(v, row, nvec, cols, w, out_, eps, scratch);
     }
-    if (threadIdx.x == 0 && abort_flag)  // copies still in flight land before the CTA exits
-        for (int s = 0; s < kRowStages; ++s)
-            if (issued[s]) mbar_wait_drain(&full[s], (issued[s] - 1) & 1, err);
+    if (threadIdx.x == 0) {
+        if (abort_flag)  // copies still in flight land before the CTA exits
+            for (int s = 0; s < STAGES; ++s)
+                if (issued[s]) mbar_wait_drain(&full[s], (issued[s] - 1) & 1, err);
+        if constexpr (BULK) bulk_wait_all();
+    }
 }
 
 // General fallback for any cols (ragged or very wide rows): three passes over the
@@ -420,15 +476,27 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
     SFn sfn = nullptr;
     const uint32_t stage_bytes = (uint32_t)(((uint64_t)cols * sizeof(T) + 127) / 128 * 128);
     const uint32_t spt = (nv + kThreads - 1) / kThreads;
-    if (sizeof(T) == 2 && vec && nv >= (uint32_t)kThreads && (uint64_t)kRowStages * stage_bytes <= 200 * 1024) {
-        if (spt <= 1) sfn = row_staged_kernel<T, 1, OP>;
-        else if (spt <= 2) sfn = row_staged_kernel<T, 2, OP>;
-        else if (spt <= 4) sfn = row_staged_kernel<T, 4, OP>;
-        else if (spt <= 8) sfn = row_staged_kernel<T, 8, OP>;
-        else if (spt <= 16) sfn = row_staged_kernel<T, 16, OP>;
+    // JADE_ROW_STAGES / JADE_ROW_STORE=bulk: measurement variants of the rows of
+    // 4 vectors per thread
+    const char *es = getenv("JADE_ROW_STAGES"), *eb = getenv("JADE_ROW_STORE");
+    const int stages = es ? std::max(2, std::min(4, atoi(es))) : 3;
+    const bool bulk = eb && !strcmp(eb, "bulk") && OP != RowOp::RmsInv;
+    if (sizeof(T) == 2 && vec && nv >= (uint32_t)kThreads && (uint64_t)stages * stage_bytes <= 200 * 1024) {
+        if (spt > 2 && spt <= 4 && (stages != 3 || bulk)) {
+            if constexpr (OP != RowOp::RmsInv) {
+                if (bulk) sfn = stages == 2 ? row_staged_kernel<T, 4, OP, 2, true> : stages == 3 ? row_staged_kernel<T, 4, OP, 3, true>
+                                                                                                 : row_staged_kernel<T, 4, OP, 4, true>;
+            }
+            if (!bulk) sfn = stages == 2 ? row_staged_kernel<T, 4, OP, 2, false> : row_staged_kernel<T, 4, OP, 4, false>;
+        } else if (spt <= 1) sfn = row_staged_kernel<T, 1, OP, 3, false>;
+        else if (spt <= 2) sfn = row_staged_kernel<T, 2, OP, 3, false>;
+        else if (spt <= 4) sfn = row_staged_kernel<T, 4, OP, 3, false>;
+        else if (spt <= 8) sfn = row_staged_kernel<T, 8, OP, 3, false>;
+        else if (spt <= 16) sfn = row_staged_kernel<T, 16, OP, 3, false>;
     }
+    const int used_stages = sfn && spt > 2 && spt <= 4 ? stages : 3;
     int sgrid = 0;
-    const int smem = kRowStages * (int)stage_bytes;
+    const int smem = used_stages * (int)stage_bytes;
     if (sfn) {
         int per_sm = 0;
         if (cudaFuncSetAttribute(sfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
@@ -437,13 +505,15 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
         else
             sgrid = (int)std::min<uint64_t>(rows, (uint64_t)per_sm * ctx->sm_count);
     }
-    if (sfn) impl = std::string("row_staged_") + dtype_name(s.dtype) + "_t" + std::to_string(kThreads);
+    if (sfn)
+        impl = std::string("row_staged_") + dtype_name(s.dtype) + "_t" + std::to_string(kThreads) + "_s" + std::to_string(used_stages) +
+               (bulk && spt > 2 && spt <= 4 ? "_bulk" : "");
     int *err = ctx->err_dev;
     return [=](cudaStream_t st, void **b) {
         const T *x = static_cast<const T *>(b[0]);
         const T *w = OP == RowOp::RmsNorm ? static_cast<const T *>(b[1]) : nullptr;
         void *out = OP == RowOp::RmsNorm ? b[2] : b[1];
-        if (sfn && reinterpret_cast<uintptr_t>(x) % 16 == 0)  // bulk copies need 16-byte aligned rows
+        if (sfn && reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0)  // bulk copies: 16-byte aligned rows
             sfn<<<sgrid, kThreads, smem, st>>>(x, w, out, rows, cols, eps, stage_bytes, err);
         else
             fn<<<grid2, threads, 0, st>>>(x, w, out, rows, cols, eps);
