@@ -605,7 +605,7 @@ def run_only(args):
         elif w == "ffma":
             res = ffma_bench(rt, args.steps, args.warmup, local)
         elif w == "mlp":
-            res = mlp_bench(rt, dist, world, args.steps, args.warmup, peaks)
+            res = mlp_bench(rt, dist, world, args.steps, args.warmup, peaks, check=(rank == 0))
         elif w == "rows":
             res = {"workload": "rows", "components": row_benches(rt, args.steps, args.warmup, peaks, local)}
         elif w == "sweep":

@@ -8,8 +8,6 @@
 // from HBM exactly once (the reference reads it 2-3 times).
 #include <algorithm>
 #include <cfloat>
-#include <cstdlib>
-#include <cstring>
 
 #include "common.cuh"
 #include "internal.hpp"
@@ -309,7 +307,7 @@ __global__ void __launch_bounds__(THREADS) row_kernel(const T *__restrict__ x, c
 
 // Row kernels with the rows staged in shared memory: thread 0 streams whole rows
 // (bulk copies counted on an mbarrier) into a ring of STAGES buffers, running up
-// to STAGES rows ahead of the arithmetic, so each SM keeps ~100 KB of reads in
+// to STAGES rows ahead of the arithmetic, so each SM keeps reads of several rows in
 // flight through the reductions and stores of the current row (the register
 // kernel has reads in flight only between its row loads and first reduction).
 // Persistent: as many CTAs as fit, rows dealt round-robin.
@@ -476,25 +474,21 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
     SFn sfn = nullptr;
     const uint32_t stage_bytes = (uint32_t)(((uint64_t)cols * sizeof(T) + 127) / 128 * 128);
     const uint32_t spt = (nv + kThreads - 1) / kThreads;
-    // JADE_ROW_STAGES / JADE_ROW_STORE=bulk: measurement variants of the rows of
-    // 4 vectors per thread
-    const char *es = getenv("JADE_ROW_STAGES"), *eb = getenv("JADE_ROW_STORE");
-    const int stages = es ? std::max(2, std::min(4, atoi(es))) : 3;
-    const bool bulk = eb && !strcmp(eb, "bulk") && OP != RowOp::RmsInv;
-    if (sizeof(T) == 2 && vec && nv >= (uint32_t)kThreads && (uint64_t)stages * stage_bytes <= 200 * 1024) {
-        if (spt > 2 && spt <= 4 && (stages != 3 || bulk)) {
-            if constexpr (OP != RowOp::RmsInv) {
-                if (bulk) sfn = stages == 2 ? row_staged_kernel<T, 4, OP, 2, true> : stages == 3 ? row_staged_kernel<T, 4, OP, 3, true>
-                                                                                                 : row_staged_kernel<T, 4, OP, 4, true>;
-            }
-            if (!bulk) sfn = stages == 2 ? row_staged_kernel<T, 4, OP, 2, false> : row_staged_kernel<T, 4, OP, 4, false>;
-        } else if (spt <= 1) sfn = row_staged_kernel<T, 1, OP, 3, false>;
-        else if (spt <= 2) sfn = row_staged_kernel<T, 2, OP, 3, false>;
-        else if (spt <= 4) sfn = row_staged_kernel<T, 4, OP, 3, false>;
-        else if (spt <= 8) sfn = row_staged_kernel<T, 8, OP, 3, false>;
-        else if (spt <= 16) sfn = row_staged_kernel<T, 16, OP, 3, false>;
+    // Results leave by bulk copies (RMSNorm, softmax) from a ring of 2 (RMSNorm) or
+    // 3 (softmax) stages; measured on B200 at 16384 x 8192 BF16 (fraction of the
+    // copy bandwidth, RMSNorm / softmax): per-thread stores from 3 stages 0.79 /
+    // 0.79-0.82, from 2 stages 0.80 / 0.77, from 4 stages 0.72 / 0.78; bulk stores
+    // from 2 stages 0.84 / 0.80, from 3 stages 0.78 / 0.85, from 4 stages 0.82 / 0.82
+    constexpr bool kBulk = OP != RowOp::RmsInv;
+    constexpr int kStages = OP == RowOp::RmsNorm ? 2 : 3;
+    if (sizeof(T) == 2 && vec && nv >= (uint32_t)kThreads && (uint64_t)kStages * stage_bytes <= 200 * 1024) {
+        if (spt <= 1) sfn = row_staged_kernel<T, 1, OP, kStages, kBulk>;
+        else if (spt <= 2) sfn = row_staged_kernel<T, 2, OP, kStages, kBulk>;
+        else if (spt <= 4) sfn = row_staged_kernel<T, 4, OP, kStages, kBulk>;
+        else if (spt <= 8) sfn = row_staged_kernel<T, 8, OP, kStages, kBulk>;
+        else if (spt <= 16) sfn = row_staged_kernel<T, 16, OP, kStages, kBulk>;
     }
-    const int used_stages = sfn && spt > 2 && spt <= 4 ? stages : 3;
+    const int used_stages = kStages;
     int sgrid = 0;
     const int smem = used_stages * (int)stage_bytes;
     if (sfn) {
@@ -507,7 +501,7 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
     }
     if (sfn)
         impl = std::string("row_staged_") + dtype_name(s.dtype) + "_t" + std::to_string(kThreads) + "_s" + std::to_string(used_stages) +
-               (bulk && spt > 2 && spt <= 4 ? "_bulk" : "");
+               (kBulk ? "_bulk" : "");
     int *err = ctx->err_dev;
     return [=](cudaStream_t st, void **b) {
         const T *x = static_cast<const T *>(b[0]);
