@@ -48,7 +48,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "GEMM & causal-attention TFLOP/s, MLP-block tokens/s at 1/2/4/8 B200"
 MLP_CHUNKS, MLP_SM_LIMIT = [0], [132]  # tensor-parallel MLP: row blocks (0 = by GPU count), GEMM CTAs
-MLP_COMM = ["nccl"]  # tensor-parallel MLP collective: nccl all-reduce or peer (NVLink scatter/reduce)
+# tensor-parallel MLP collective: nccl all-reduce, peer (NVLink scatter/reduce) or
+# auto = peer at 2 and 4 GPUs (measured faster there), nccl otherwise
+MLP_COMM = ["auto"]
 B, H, S, D = 4, 16, 2048, 128
 
 
@@ -308,11 +310,22 @@ def row_benches(rt, steps, warmup, peaks, device=0):
     return out
 
 
+def mlp_comm(world):
+    """The MLP collective for `world` ranks (--mlp-comm; auto = peer at 2 and 4)."""
+    if world <= 1:
+        return "nccl"
+    if MLP_COMM[0] == "auto":
+        return "peer" if world in (2, 4) else "nccl"
+    return MLP_COMM[0]
+
+
 def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     """T=8192, d=4096, ffn=14336 residual MLP, tensor parallel
-    over the ranks with one NCCL all-reduce after the down projection."""
+    over the ranks; the partial outputs are summed by an NCCL all-reduce or by the
+    NVLink peer scatter/reduce fused into the down projection (mlp_comm)."""
     from jade_compute_b200 import parallel
     from jade_compute_b200.mlp import ResidualMLP
+    from jade_compute_b200.runtime import JadeError
     T, d, ffn = 8192, 4096, 14336
     rank = dist.get_rank() if dist is not None else 0
     if world > 1:
@@ -324,18 +337,44 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
     # leave SMs for NCCL. Smaller blocks cost GEMM wave efficiency: one block measured
     # faster than four at 2 GPUs (7.0 vs 6.3 M tokens/s) and than two at 4 GPUs
     # (11.1 vs 9.8), so the default is one block
-    comm = MLP_COMM[0] if world > 1 else "nccl"
+    comm = mlp_comm(world)
+
+    def build(comm):
+        if comm == "peer":
+            # the down GEMM scatters its partial rows to their owners over NVLink,
+            # owners reduce and push their rows to every rank (csrc/peer.cu)
+            chunks, sm_limit = 1, 0
+        else:
+            chunks = MLP_CHUNKS[0] if MLP_CHUNKS[0] > 0 else 1
+            sm_limit = MLP_SM_LIMIT[0] if chunks > 1 else 0
+        mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit, comm=comm)
+        if comm == "peer":
+            mlp.attach(dist)  # raises on every rank if any rank cannot map the peers' buffers
+        mlp.fill_synthetic(seed=11)
+        return mlp, chunks, sm_limit
+
+    fallback = None
+    try:
+        mlp, chunks, sm_limit = build(comm)
+        failure = None
+    except JadeError as e:
+        mlp, failure = None, e
     if comm == "peer":
-        # the down GEMM scatters its partial rows to their owners over NVLink,
-        # owners reduce and push their rows to every rank (csrc/peer.cu)
-        chunks, sm_limit = 1, 0
-    else:
-        chunks = MLP_CHUNKS[0] if MLP_CHUNKS[0] > 0 else 1
-        sm_limit = MLP_SM_LIMIT[0] if chunks > 1 else 0
-    mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit, comm=comm)
-    if comm == "peer":
-        mlp.attach(dist)
-    mlp.fill_synthetic(seed=11)
+        # the peer path's warm-up also decides: a rank whose step fails (a bounded
+        # wait that expired) makes every rank fall back to NCCL together
+        if mlp is not None:
+            try:
+                rt.execute(mlp.jobs(), repeats=max(warmup, 3))
+            except JadeError as e:
+                failure = e
+        if not parallel.all_true(dist, failure is None):
+            fallback = str(failure or "another rank failed")[:200]
+            if mlp is not None:
+                mlp.release()
+            comm = "nccl"
+            mlp, chunks, sm_limit = build(comm)
+    elif failure is not None:
+        raise failure
     jobs = mlp.jobs()
     lanes = chunks > 1
     rt.execute(jobs, repeats=max(warmup, 3), streams=lanes)
@@ -368,6 +407,7 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
            "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "n_gpus": world, "scaling": "strong",
            "tflops": flops / (ms * 1e-3) / 1e12, "job_ms": job_ms,
            "row_blocks": chunks, "gemm_sm_limit": sm_limit or None, "collective": comm if world > 1 else None,
+           "collective_fallback": fallback,
            "roofline": {"bound": "tensor", "achieved": per_gpu_tflops, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": per_gpu_tflops / peaks["bf16_sustained"], "peak_source": peaks["source"] + " sustained bf16"},
            "kernels": [k.info.get("impl") for k, _ in jobs], "clocks": clk.summary()}
@@ -538,7 +578,7 @@ def mlp_error(rt, mlp, world, seed, rows=(0, 1, 4097, 8191)):
     rms = float(np.sqrt((ref ** 2).mean()))
     return {"rows": len(rows), "max_err_over_m": float((err / mag).max()), "max_err_over_rms": float(err.max() / rms),
             "max_err_over_ref_bf16_ulps": float((err / np.maximum(np.abs(ref), rms * 1e-3)).max() / 2.0 ** -8),
-            "tp": world, "collective": (MLP_COMM[0] if world > 1 else None),
+            "tp": world, "collective": mlp.comm if world > 1 else None,
             "partials_dtype": "bf16"}
 
 
@@ -763,8 +803,9 @@ def _main(out_fd):
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--mlp-chunks", type=int, default=MLP_CHUNKS[0],
                     help="row blocks of the tensor-parallel MLP (0 = one block)")
-    ap.add_argument("--mlp-comm", choices=["nccl", "peer"], default=MLP_COMM[0],
-                    help="tensor-parallel MLP collective: NCCL all-reduce or NVLink peer scatter/reduce")
+    ap.add_argument("--mlp-comm", choices=["auto", "nccl", "peer"], default=MLP_COMM[0],
+                    help="tensor-parallel MLP collective: NCCL all-reduce, NVLink peer scatter/reduce, or auto "
+                         "(peer at 2 and 4 GPUs, NCCL otherwise)")
     ap.add_argument("--mlp-sm-limit", type=int, default=MLP_SM_LIMIT[0],
                     help="persistent CTAs of the tensor-parallel MLP's GEMMs (0 = one per SM)")
     ap.add_argument("--only", choices=["attention", "attention_full", "gemm", "ffma", "mlp", "rows", "sweep"] + KERNEL_CASES,

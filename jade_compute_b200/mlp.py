@@ -113,6 +113,17 @@ class ResidualMLP:
             raise ValueError("attach is for comm='peer'")
         share_buffers(self.rt, dist, [*self.recvs, *self.ys, self.flags])
 
+    def release(self) -> None:
+        """Frees the block's buffers (detaching peer mappings) and kernels."""
+        bufs = [*self.xs, *self.invs, *self.hs, *self.ys, self.wgu, self.wd]
+        if self.comm == "peer":
+            bufs += [*self.recvs, self.flags]
+        for b in bufs:
+            b.free()
+        for k in (self.k_inv, self.k_up, self.k_down, self.k_ar, self.k_reduce, self.k_gather):
+            if k is not None:
+                k.release()
+
     # single-block views (chunks == 1)
     @property
     def x(self):

@@ -87,13 +87,42 @@ def all_gather_bytes(dist, payload: bytes) -> list:
     return [bytes(t.tolist()) for t in out]
 
 
+def all_true(dist, flag: bool) -> bool:
+    """True when `flag` holds on every rank (a collective over the CPU group)."""
+    if dist is None:
+        return bool(flag)
+    import torch
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
 def share_buffers(rt: "_rt.Runtime", dist, buffers) -> None:
     """Attaches each buffer to its counterparts on every rank (CUDA IPC handles
     exchanged over the CPU group; every rank passes the same sequence of
-    same-sized buffers). Single process: attaches with one rank."""
+    same-sized buffers). Single process: attaches with one rank.
+
+    Every rank takes the same collective steps whatever fails: the handles of all
+    buffers travel in one exchange with a status byte, each rank maps them
+    locally, and the ranks then agree on the outcome; if exporting or mapping
+    failed on any rank, every rank raises JadeError (buffers mapped so far stay
+    attached until they are freed)."""
     rank = dist.get_rank() if dist is not None else 0
-    for buf in buffers:
-        handles = all_gather_bytes(dist, rt.peer_handle(buf)) if dist is not None else [b"\0" * 64]
-        rt.peer_attach(buf, handles, rank)
-    if dist is not None:
-        dist.barrier()
+    buffers = list(buffers)
+    failure = None
+    try:
+        mine = b"".join(rt.peer_handle(b) for b in buffers)
+    except _rt.JadeError as e:
+        mine, failure = b"\0" * (64 * len(buffers)), e
+    payload = bytes([failure is None]) + mine
+    every = all_gather_bytes(dist, payload) if dist is not None else [payload]
+    if failure is None and not all(p[0] for p in every):
+        failure = _rt.JadeError(_rt.JR_EINVAL, "a rank could not export its peer handles")
+    if failure is None:
+        try:
+            for i, buf in enumerate(buffers):
+                rt.peer_attach(buf, [p[1 + 64 * i:1 + 64 * (i + 1)] for p in every], rank)
+        except _rt.JadeError as e:
+            failure = e
+    if not all_true(dist, failure is None):
+        raise failure or _rt.JadeError(_rt.JR_EINVAL, "another rank could not attach its peer buffers")

@@ -37,6 +37,36 @@ def _worker(rank, world, port, scenario, q):
                 q.put((rank, "detected: " + type(e).__name__))
             return
         dist = P.init_process_group(timeout_s=10 if scenario != "leave_between_steps" else 5)
+        if scenario.startswith("share"):
+            # peer-buffer sharing agrees on failure: a rank that cannot export (or
+            # map) its handles makes every rank raise, with no collective left waiting
+            from jade_compute_b200.runtime import JadeError
+
+            class FakeRuntime:
+                def __init__(self):
+                    self.attached = []
+
+                def peer_handle(self, buf):
+                    if scenario == "share_export_fails" and rank == 1:
+                        raise JadeError(1, "export refused")
+                    return bytes([rank, buf]) + b"\0" * 62
+
+                def peer_attach(self, buf, handles, r):
+                    if scenario == "share_attach_fails" and rank == 0:
+                        raise JadeError(2, "map refused")
+                    assert [h[:2] for h in handles] == [bytes([q, buf]) for q in range(world)] and r == rank
+                    self.attached.append(buf)
+
+            rt = FakeRuntime()
+            try:
+                P.share_buffers(rt, dist, [7, 8, 9])
+                result = "attached " + ",".join(map(str, rt.attached))
+            except JadeError as e:
+                result = "raised " + e.message
+            dist.barrier()  # both ranks are still in step: no collective was left waiting
+            dist.destroy_process_group()
+            q.put((rank, result))
+            return
         if scenario == "leave_between_steps":
             dist.barrier()  # step 1 completes on both ranks
             if rank == 1:
@@ -122,3 +152,15 @@ def test_rank_that_leaves_between_steps_is_detected_on_host():
     out = _run("leave_between_steps")
     assert out[1] == "left"
     assert out[0].startswith("detected"), out
+
+
+def test_peer_buffer_sharing_attaches_every_buffer():
+    assert _run("share_ok") == {0: "attached 7,8,9", 1: "attached 7,8,9"}
+
+
+@pytest.mark.parametrize("scenario", ["share_export_fails", "share_attach_fails"])
+def test_peer_buffer_sharing_fails_on_every_rank_together(scenario):
+    out = _run(scenario)
+    assert all(v.startswith("raised") for v in out.values()), out
+    failing = 1 if scenario == "share_export_fails" else 0
+    assert "refused" in out[failing], out
