@@ -122,6 +122,12 @@ template <>
 __device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16 *dst, const float (&v)[32], int valid, bool vec_ok) {
     store32_16(dst, v, valid, vec_ok);
 }
+// Two values rounded to a 16-bit type, packed low | high << 16.
+template <typename T16>
+__device__ __forceinline__ uint32_t pack16_out(float lo, float hi) {
+    if constexpr (std::is_same<T16, __nv_bfloat16>::value) return pack_bf16(lo, hi);
+    else return pack_f16(lo, hi);
+}
 // Four consecutive values of a row (16 B of FP32, 8 B of 16-bit types).
 template <typename TOut>
 __device__ __forceinline__ void store4(TOut *dst, const float (&v)[4], int valid, bool vec_ok) {
@@ -349,6 +355,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int col = c0 + c;
                     if (row < args.M && col < args.N)
                         store32<TOut>(out + (size_t)row * args.N + col, h, args.N - col, (args.N % 8) == 0);
+                }
+            } else if constexpr (sizeof(TOut) == 2 && (kEpi == kEpiNone || kEpi == kEpiScatter)) {
+                // 16-bit output: the warp's 32 rows x 64 columns are rounded first and
+                // go through its padded shared-memory block as packed pairs, so that each
+                // lane stores 16 bytes and each row segment of a store instruction is one
+                // whole 128-byte line (local or, for the scatter, a peer's memory)
+                uint32_t *blk = reinterpret_cast<uint32_t *>(smem + kStages * kStageBytes + 256) + (warp - 2) * (32 * 33);
+                const int c0 = tn * BN, row0 = tm * BM + quarter * 32;
+                const int c8 = (lane & 7) * 8;  // this lane's 8 columns; its row in each group of 4 is r_sub
+                const bool vec_ok = (args.N % 8) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 64) {
+                    const int col = c0 + c;
+                    if (col >= args.N) break;  // uniform across the warp
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c + 32 * h, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            blk[lane * 33 + 16 * h + j] = pack16_out<TOut>(__uint_as_float(r[2 * j]) * scale, __uint_as_float(r[2 * j + 1]) * scale);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rl = i * 4 + r_sub, grow = row0 + rl, gcol = col + c8;
+                        if (grow < args.M && gcol < args.N) {
+                            const uint32_t *src = blk + rl * 33 + (c8 >> 1);
+                            const uint4 u = make_uint4(src[0], src[1], src[2], src[3]);
+                            TOut *dst = out + (size_t)grow * args.N + gcol;
+                            if (vec_ok) {
+                                *reinterpret_cast<uint4 *>(dst) = u;
+                            } else {
+                                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                                for (int e = 0; e < 8; ++e)
+                                    if (gcol + e < args.N) reinterpret_cast<uint16_t *>(dst)[e] = (uint16_t)(w[e >> 1] >> (16 * (e & 1)));
+                            }
+                        }
+                    }
+                    __syncwarp();  // the block is read before the next chunk overwrites it
                 }
             } else {
                 // The warp's 32 rows x 32 columns go through its padded shared-memory

@@ -59,14 +59,29 @@ def test_tc_gemm_fp32_out(rt, dtype, b_nk, mnk):
     assert rc == 0, (rc, v.first_bad_index, v.max_scaled_error, kern.info["impl"])
 
 
+# 16-bit outputs leave the epilogue in 64-column chunks of packed pairs: whole
+# chunks, a partial last chunk (N % 64 != 0), a ragged row (N % 8 != 0: element
+# stores) and ragged M
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
-def test_tc_gemm_16bit_out(rt, dtype):
-    m, n, k = 384, 512, 640
-    a, b, af, bf = operands(rt, m, n, k, dtype, False, seed=3)
+@pytest.mark.parametrize("m,n,k,b_nk,row_scale", [(384, 512, 640, False, False), (130, 1000, 128, True, False),
+                                                 (200, 300, 256, True, False), (257, 264, 64, True, True)])
+def test_tc_gemm_16bit_out(rt, dtype, m, n, k, b_nk, row_scale):
+    a, b, af, bf = operands(rt, m, n, k, dtype, b_nk, seed=3 + n)
     out = rt.alloc(m * n, dtype)
-    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": dtype, "out_dtype": dtype})
-    rt.execute([(kern, [a, b, out])])
+    spec = {"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": dtype, "out_dtype": dtype,
+            "b_layout": "nk" if b_nk else "kn"}
+    bufs = [a, b]
+    if row_scale:
+        spec["row_scale"] = True
+        sc = rt.alloc(m)
+        rt.fill(sc, "uniform", seed=5, stream=4, lo=0.5, hi=2.0)
+        bufs.append(sc)
+    kern = rt.compile(spec)
+    assert kern.info["path"] == "tcgen05", kern.info
+    rt.execute([(kern, bufs + [out])])
     exp = O.gemm_reference(m, n, k, af, bf)
+    if row_scale:
+        exp = (exp.reshape(m, n) * rt.download(sc).astype(np.float64)[:, None]).ravel()
     scale = np.abs(exp).max()
     rc, r = O.compare(rt.download_f32(out), exp, 2e-3 * scale, 2 ** -8)
     assert rc == 0, r.max_abs_error
