@@ -349,7 +349,11 @@ def mlp_bench(rt, dist, world, steps, warmup, peaks, check=False):
             sm_limit = MLP_SM_LIMIT[0] if chunks > 1 else 0
         mlp = ResidualMLP(rt, T, d, ffn, tp=world, rank=rank, chunks=chunks, sm_limit=sm_limit, comm=comm)
         if comm == "peer":
-            mlp.attach(dist)  # raises on every rank if any rank cannot map the peers' buffers
+            try:
+                mlp.attach(dist)  # raises on every rank if any rank cannot map the peers' buffers
+            except JadeError:
+                mlp.release()
+                raise
         mlp.fill_synthetic(seed=11)
         return mlp, chunks, sm_limit
 

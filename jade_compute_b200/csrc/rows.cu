@@ -179,9 +179,6 @@ template <> struct Vec<float> {
         const float4 v = *reinterpret_cast<const float4 *>(p);
         d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
     }
-    __device__ static void unpack(uint4 v, float *d) {
-        d[0] = __uint_as_float(v.x); d[1] = __uint_as_float(v.y); d[2] = __uint_as_float(v.z); d[3] = __uint_as_float(v.w);
-    }
     __device__ static void store_shared(float *p, const float *d) { *reinterpret_cast<float4 *>(p) = make_float4(d[0], d[1], d[2], d[3]); }
     __device__ static void store(float *p, const float *d) {
         __stcs(reinterpret_cast<float4 *>(p), make_float4(d[0], d[1], d[2], d[3]));
@@ -219,13 +216,10 @@ enum class RowOp { RmsNorm, Softmax, RmsInv };
 // exponentials on the MUFU unit, exp_neg);
 // RMSNorm = sum of squares, scale by inv*w; RmsInv = the per-row inverse RMS only.
 // SINK: results go to `sink` (the row's shared-memory stage, written back by bulk
-// copies) instead of global memory; WPRE: the RMSNorm weights come from `wpre`, the
-// thread's weight vectors held in registers across rows (the columns of a thread
-// are the same in every row).
-template <typename T, int NV, RowOp OP, int THREADS, bool SINK = false, bool WPRE = false>
+// copies) instead of global memory.
+template <typename T, int NV, RowOp OP, int THREADS, bool SINK = false>
 __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t row, uint32_t nvec, uint32_t cols, const T *__restrict__ w,
-                                            void *__restrict__ out_, float eps, float *scratch, T *sink = nullptr,
-                                            const uint4 *wpre = nullptr) {
+                                            void *__restrict__ out_, float eps, float *scratch, T *sink = nullptr) {
     constexpr int N = Vec<T>::N;
     auto put = [&](uint32_t c, const float *d) {
         if constexpr (SINK) Vec<T>::store_shared(sink + (uint64_t)c * N, d);
@@ -276,8 +270,7 @@ __device__ __forceinline__ void row_compute(float (&v)[NV][Vec<T>::N], uint32_t 
                 const uint32_t c = threadIdx.x + j * THREADS;
                 if (c < nvec) {
                     float wv[N];
-                    if constexpr (WPRE) Vec<T>::unpack(wpre[j], wv);
-                    else Vec<T>::load_keep(w + (uint64_t)c * N, wv);
+                    Vec<T>::load_keep(w + (uint64_t)c * N, wv);
 #pragma unroll
                     for (int e = 0; e < N; ++e) v[j][e] = v[j][e] * inv * wv[e];
                     put(c, v[j]);
@@ -316,8 +309,7 @@ __global__ void __launch_bounds__(THREADS) row_kernel(const T *__restrict__ x, c
 // copies (one thread issues them; the copy engine writes whole lines), instead of
 // 16-byte stores from every thread. A stage is then refilled one iteration later,
 // once its store has read it out, so STAGES - 1 rows are in flight ahead of the
-// arithmetic. RMSNorm rows of up to 4 vectors per thread keep the thread's weights
-// in registers for all rows.
+// arithmetic.
 constexpr uint32_t kRowChunk = 8192;  // bytes per bulk copy
 
 template <typename T, int NV, RowOp OP, int STAGES, bool BULK>
@@ -328,17 +320,8 @@ __global__ void __launch_bounds__(kThreads) row_staged_kernel(const T *__restric
     __shared__ uint64_t full[STAGES];
     __shared__ int abort_flag;
     constexpr int N = Vec<T>::N;
-    constexpr bool kWpre = false;
     static_assert(!BULK || OP != RowOp::RmsInv, "RmsInv writes one value per row");
     const uint32_t nvec = cols / N, row_bytes = cols * (uint32_t)sizeof(T);
-    uint4 wpre[kWpre ? NV : 1];
-    if constexpr (kWpre) {
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-            const uint32_t c = threadIdx.x + j * kThreads;
-            if (c < nvec) wpre[j] = __ldg(reinterpret_cast<const uint4 *>(w + (uint64_t)c * N));
-        }
-    }
     int issued[STAGES] = {};  // thread 0: rows loaded into each stage
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
@@ -377,11 +360,11 @@ __global__ void __launch_bounds__(kThreads) row_staged_kernel(const T *__restric
                 const uint64_t next = row + (uint64_t)STAGES * gridDim.x;
                 if (next < rows) issue((uint32_t)next, s);
             }
-            row_compute<T, NV, OP, kThreads, false, kWpre>(v, row, nvec, cols, w, out_, eps, scratch, nullptr, wpre);
+            row_compute<T, NV, OP, kThreads, false>(v, row, nvec, cols, w, out_, eps, scratch);
         } else {
             // every thread overwrites only the vectors it read, so no barrier is
             // needed between the loads above and these stores
-            row_compute<T, NV, OP, kThreads, true, kWpre>(v, row, nvec, cols, w, out_, eps, scratch, xr, wpre);
+            row_compute<T, NV, OP, kThreads, true>(v, row, nvec, cols, w, out_, eps, scratch, xr);
             fence_proxy_async();  // this thread's shared stores, visible to the bulk copies
             __syncthreads();
             if (threadIdx.x == 0) {
