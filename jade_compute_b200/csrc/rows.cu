@@ -461,10 +461,14 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
     // 3 (softmax) stages; measured on B200 at 16384 x 8192 BF16 (fraction of the
     // copy bandwidth, RMSNorm / softmax): per-thread stores from 3 stages 0.79 /
     // 0.79-0.82, from 2 stages 0.80 / 0.77, from 4 stages 0.72 / 0.78; bulk stores
-    // from 2 stages 0.84 / 0.80, from 3 stages 0.78 / 0.85, from 4 stages 0.82 / 0.82
+    // from 2 stages 0.84 / 0.80, from 3 stages 0.78 / 0.85, from 4 stages 0.82 / 0.82.
+    // FP32 rows (16384 x 8192) stay on the register kernel for RMSNorm (0.91-0.92 vs
+    // 0.86-0.87 staged) and are staged for softmax (0.87 vs 0.85), with rows of up to
+    // 32 KB (at least two CTAs per SM)
     constexpr bool kBulk = OP != RowOp::RmsInv;
     constexpr int kStages = OP == RowOp::RmsNorm ? 2 : 3;
-    if (sizeof(T) == 2 && vec && nv >= (uint32_t)kThreads && (uint64_t)kStages * stage_bytes <= 200 * 1024) {
+    const bool staged = sizeof(T) == 2 || (OP == RowOp::Softmax && stage_bytes <= 32 * 1024);
+    if (staged && vec && nv >= (uint32_t)kThreads && (uint64_t)kStages * stage_bytes <= 200 * 1024) {
         if (spt <= 1) sfn = row_staged_kernel<T, 1, OP, kStages, kBulk>;
         else if (spt <= 2) sfn = row_staged_kernel<T, 2, OP, kStages, kBulk>;
         else if (spt <= 4) sfn = row_staged_kernel<T, 4, OP, kStages, kBulk>;

@@ -240,13 +240,18 @@ def test_row_kernels(rt, rows, cols, dtype):
     assert rc == 0
 
 
-@pytest.mark.parametrize("rows,cols,dtype,path", [(2000, 8192, "bf16", "row_staged_"), (3001, 4096, "bf16", "row_staged_"),
-                                                  (700, 32768, "bf16", "row_staged_"), (1500, 2048, "bf16", "row_staged_"),
-                                                  (2000, 8192, "fp32", "row_register_"), (700, 16384, "fp32", "row_register_")])
-def test_row_kernels_many_rows(rt, rows, cols, dtype, path):
-    # many rows per CTA: 16-bit rows staged through shared memory by bulk copies
-    # (several rows per ring position), FP32 rows register-resident (the kernel
-    # name says which path ran)
+STAGED, REGISTER = "row_staged_", "row_register_"
+
+
+@pytest.mark.parametrize("rows,cols,dtype,paths", [(2000, 8192, "bf16", (STAGED,) * 3), (3001, 4096, "bf16", (STAGED,) * 3),
+                                                   (700, 32768, "bf16", (STAGED,) * 3), (1500, 2048, "bf16", (STAGED,) * 3),
+                                                   (2000, 8192, "fp32", (REGISTER, STAGED, REGISTER)),
+                                                   (700, 16384, "fp32", (REGISTER,) * 3)])
+def test_row_kernels_many_rows(rt, rows, cols, dtype, paths):
+    # many rows per CTA: 16-bit rows and FP32 softmax rows up to 32 KB staged
+    # through shared memory by bulk copies (several rows per ring position), the
+    # other FP32 rows register-resident (the kernel name says which path ran;
+    # paths = rms_norm, softmax, rms_inv)
     x = rt.alloc(rows * cols, dtype)
     w = rt.alloc(cols, dtype)
     rt.fill(x, "normal", seed=5, lo=0.0, hi=2.0)
@@ -256,7 +261,7 @@ def test_row_kernels_many_rows(rt, rows, cols, dtype, path):
     base = {"rows": rows, "cols": cols, "dtype": dtype}
     kerns = [rt.compile({"op": "rms_norm", "epsilon": 1e-6, **base}), rt.compile({"op": "softmax", **base}),
              rt.compile({"op": "rms_inv", "epsilon": 1e-6, **base})]
-    for k in kerns:
+    for k, path in zip(kerns, paths):
         assert k.info["impl"].startswith(path), k.info
     rt.execute([(kerns[0], [x, w, y]), (kerns[1], [x, p]), (kerns[2], [x, inv])], repeats=2)
     eps = float(np.float32(1e-6))
