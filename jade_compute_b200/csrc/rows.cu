@@ -448,11 +448,12 @@ LaunchFn row_launch(Context *ctx, const Spec &s, std::string &impl) {
     const int grid2 = threads == 128 ? grid_for(ctx, rows, 1, 32) : grid;
     impl = std::string(fn == (KFn)row_kernel_general<T, OP> ? "row_general_" : "row_register_") + dtype_name(s.dtype) + "_t" +
            std::to_string(threads);
-    // Staged variant for 16-bit rows (whole rows of at least one vector per thread
-    // whose three stages fit in shared memory). Measured on B200 at 16384 x 8192:
-    // BF16 RMSNorm 5.23 vs 4.75 TB/s and softmax 5.23 vs 4.92 TB/s for the staged
-    // kernel; FP32 rows (twice the bytes per element) run faster on the register
-    // kernel (6.18 vs 6.02 and 5.76 vs 5.29 TB/s).
+    // Staged variant (whole rows of at least one vector per thread whose stages fit
+    // in shared memory) for 16-bit rows and FP32 softmax rows. Measured on B200 at
+    // 16384 x 8192 with per-thread stores, before the bulk-copy stores: BF16 RMSNorm
+    // 5.23 vs 4.75 TB/s and softmax 5.23 vs 4.92 TB/s for the staged kernel; FP32
+    // rows (twice the bytes per element) then ran faster on the register kernel
+    // (6.18 vs 6.02 and 5.76 vs 5.29 TB/s).
     using SFn = void (*)(const T *, const T *, void *, uint32_t, uint32_t, float, uint32_t, int *);
     SFn sfn = nullptr;
     const uint32_t stage_bytes = (uint32_t)(((uint64_t)cols * sizeof(T) + 127) / 128 * 128);
