@@ -623,18 +623,19 @@ def kernel_case(rt, case):
         h, wd, x, y = bufs((T * f, "bf16"), (d * f, "bf16"), (T * d, "bf16"), (T * d, "bf16"))
         return [(rt.compile({"op": "gemm", "m": T, "n": d, "k": f, "tiled": True, "dtype": "bf16", "b_layout": "nk",
                              "out_dtype": "bf16", "epilogue": "residual"}), [h, wd, x, y])]
-    if case in ("rms_bf16", "softmax_bf16"):  # BASELINE configs[2] row kernels on BF16 rows, 16384 x 8192
+    if case in ("rms_bf16", "softmax_bf16", "softmax_fp32"):  # BASELINE configs[2] row kernels, 16384 x 8192
         R, C = 16384, 8192
         if case == "rms_bf16":
             x, w, y = bufs((R * C, "bf16"), (C, "bf16"), (R * C, "bf16"))
             return [(rt.compile({"op": "rms_norm", "rows": R, "cols": C, "epsilon": 1e-6, "dtype": "bf16"}), [x, w, y])]
-        x, y = bufs((R * C, "bf16"), (R * C, "bf16"))
-        return [(rt.compile({"op": "softmax", "rows": R, "cols": C, "dtype": "bf16"}), [x, y])]
+        dt = "fp32" if case == "softmax_fp32" else "bf16"
+        x, y = bufs((R * C, dt), (R * C, dt))
+        return [(rt.compile({"op": "softmax", "rows": R, "cols": C, "dtype": dt}), [x, y])]
     raise SystemExit(f"unknown kernel case {case}")
 
 
 KERNEL_CASES = ["tf32_kn", "ffma512", "ffma2048", "swiglu", "axpy", "add", "swiglu_bf16", "attention_fp32", "mlp_down_k1792",
-                "rms_bf16", "softmax_bf16"]
+                "rms_bf16", "softmax_bf16", "softmax_fp32"]
 
 
 def run_only(args):
