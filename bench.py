@@ -600,6 +600,10 @@ def kernel_case(rt, case):
         m = 4096
         a, b, c = bufs((m * m, "tf32"), (m * m, "tf32"), (m * m, "fp32"))
         return [(rt.compile({"op": "gemm", "m": m, "n": m, "k": m, "tiled": True, "dtype": "tf32"}), [a, b, c])]
+    if case == "gemm_bf16_longk":  # 32 output tiles, K = 8192: split-K (4 ranges) and its reduction
+        m, k = 1024, 8192
+        a, b, c = bufs((m * k, "bf16"), (k * m, "bf16"), (m * m, "fp32"))
+        return [(rt.compile({"op": "gemm", "m": m, "n": m, "k": k, "tiled": True, "dtype": "bf16", "b_layout": "nk"}), [a, b, c])]
     if case in ("ffma512", "ffma2048"):  # FP32 FFMA GEMM (BASELINE configs[0] and a larger square)
         m = 512 if case == "ffma512" else 2048
         a, b, c = bufs((m * m, "fp32"), (m * m, "fp32"), (m * m, "fp32"))
@@ -634,7 +638,7 @@ def kernel_case(rt, case):
     raise SystemExit(f"unknown kernel case {case}")
 
 
-KERNEL_CASES = ["tf32_kn", "ffma512", "ffma2048", "swiglu", "axpy", "add", "swiglu_bf16", "attention_fp32", "mlp_down_k1792",
+KERNEL_CASES = ["tf32_kn", "gemm_bf16_longk", "ffma512", "ffma2048", "swiglu", "axpy", "add", "swiglu_bf16", "attention_fp32", "mlp_down_k1792",
                 "rms_bf16", "softmax_bf16", "softmax_fp32"]
 
 

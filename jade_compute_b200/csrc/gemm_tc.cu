@@ -48,6 +48,11 @@ struct GemmArgs {
     const void *residual;
     int M, N, K;  // N = output columns
     int tiles_m, tiles_n, num_tiles, kblocks;
+    // split-K: work unit u is tile u % num_tiles over K-blocks [s * kb_per, (s + 1) * kb_per)
+    // of split s = u / num_tiles, written to out + s * split_stride elements (FP32
+    // partials that a second kernel sums in split order); ksplit = 1 otherwise
+    int ksplit, kb_per, num_units;
+    long long split_stride;
     int group_m;  // M-blocks per raster group (tile_coords)
     int *err;
     // scatter epilogue: every rank's receive buffer; the rows of rank r are
@@ -253,11 +258,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             bool issued[kStages] = {};
             uint32_t last_phase[kStages] = {};
-            for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+            for (int u = blockIdx.x; u < args.num_units && !*abort_flag; u += gridDim.x) {
+                const int t = u % args.num_tiles, kb0 = (u / args.num_tiles) * args.kb_per;
                 int tm, tn;
                 tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, args.m_rotate, tm, tn);
                 const int m0 = tm * BM, nb0 = tn * BN;  // B rows (nk) or columns (kn) of this tile
-                for (int kb = 0; kb < args.kblocks; ++kb) {
+                for (int kb = kb0; kb < min(args.kblocks, kb0 + args.kb_per); ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, err, kErrWaitSmemEmpty)) break;
                     uint8_t *sa = smem + stage * kStageBytes;
                     uint8_t *sb = sa + kStageA;
@@ -285,12 +291,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int t = blockIdx.x; t < args.num_tiles && !__any_sync(0xffffffffu, *abort_flag); t += gridDim.x) {
+            for (int u = blockIdx.x; u < args.num_units && !__any_sync(0xffffffffu, *abort_flag); u += gridDim.x) {
+                const int kb0 = (u / args.num_tiles) * args.kb_per;
                 if (!mbar_wait_warp(&acc_empty[acc], acc_phase ^ 1, abort_flag, err, kErrWaitAccEmpty)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 bool ok = true;
-                for (int kb = 0; kb < args.kblocks; ++kb) {
+                for (int kb = kb0; kb < min(args.kblocks, kb0 + args.kb_per); ++kb) {
                     if (!mbar_wait_warp(&full[stage], phase, abort_flag, err, kErrWaitTmaFull)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * kStageBytes);
@@ -301,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint64_t bdesc;
                         if constexpr (kBmn) bdesc = sdesc_sw128(sb + k * UK * 128, kBoxBytesB, 1024);
                         else bdesc = sdesc_sw128(sb + k * 32, 16, 1024);
-                        umma<kFmt == 2>(d_tmem, adesc, bdesc, kIdesc, (kb | k) != 0);
+                        umma<kFmt == 2>(d_tmem, adesc, bdesc, kIdesc, (kb != kb0) | (k != 0));
                     }
                     umma_commit(&empty[stage]);  // frees the stage when these MMAs finish reading it
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
@@ -321,7 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         const int r_sub = lane >> 3, c_sub = (lane & 7) * 4;  // this lane's row in each group of 4, its columns
         ResidualChunk<TOut> res_next;
-        for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+        for (int u = blockIdx.x; u < args.num_units && !*abort_flag; u += gridDim.x) {
+            const int t = u % args.num_tiles;
             int tm, tn;
             tile_coords(t, args.tiles_m, args.tiles_n, args.group_m, args.m_rotate, tm, tn);
             if constexpr (kEpi == kEpiResidual)  // the residual does not wait for the MMAs: fetch chunk 0 now
@@ -332,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = tm * BM + row_in_tile;
             const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
             const float scale = (kRowScale && row < args.M) ? args.row_scale[row] : 1.0f;
-            TOut *out = static_cast<TOut *>(args.out);
+            TOut *out = static_cast<TOut *>(args.out) + (u / args.num_tiles) * args.split_stride;
             if constexpr (kEpi == kEpiScatter) {
                 // the tile's rows belong to one rank: its receive buffer, this rank's slot
                 const int owner = (tm * BM) / args.rows_per_rank;
@@ -480,7 +488,7 @@ bool make_map(CUtensorMap *map, CUtensorMapDataType dt, int eb, const void *ptr,
 }
 
 template <int kEB, uint32_t kFmt, bool kBmn, typename TOut, int kEpi, bool kRowScale>
-LaunchFn tc_launch(Context *ctx, const Spec &s) {
+LaunchFn tc_launch(Context *ctx, const Spec &s, int ksplit = 1) {
     auto kernel = gemm_tc_kernel<kEB, kFmt, kBmn, TOut, kEpi, kRowScale>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
         throw IrError("cannot reserve shared memory for the tcgen05 GEMM");
@@ -498,7 +506,11 @@ LaunchFn tc_launch(Context *ctx, const Spec &s) {
     base.kblocks = (int)((s.k + (128 / kEB) - 1) / (128 / kEB));
     base.group_m = raster_group(base.tiles_m, s.k, kEB);
     base.err = ctx->err_dev;
-    const int grid = std::min(base.num_tiles, s.sm_limit ? std::min<int>((int)s.sm_limit, ctx->sm_count) : ctx->sm_count);
+    base.ksplit = ksplit;
+    base.kb_per = (base.kblocks + ksplit - 1) / ksplit;
+    base.num_units = base.num_tiles * ksplit;
+    base.split_stride = ksplit > 1 ? (long long)s.m * s.n : 0;
+    const int grid = std::min(base.num_units, s.sm_limit ? std::min<int>((int)s.sm_limit, ctx->sm_count) : ctx->sm_count);
     const uint32_t ranks = s.ranks, rank = s.rank;
     if (kEpi == kEpiScatter) {
         base.rows_per_rank = (int)(s.m / s.ranks);
@@ -531,6 +543,85 @@ LaunchFn tc_launch(Context *ctx, const Spec &s) {
     };
 }
 
+// Device workspace owned by a compiled kernel, released with it.
+struct Workspace {
+    void *ptr = nullptr;
+    int device = 0;
+    ~Workspace() {
+        if (ptr) {
+            cudaSetDevice(device);
+            cudaFree(ptr);
+        }
+    }
+};
+
+// out = sum over s of part[s] (in split order, FP32), rounded once to TOut.
+template <typename TOut>
+__global__ void splitk_reduce(const float *__restrict__ part, TOut *__restrict__ out, long long n, int ksplit, long long stride, bool vec) {
+    const long long step = (long long)gridDim.x * blockDim.x;
+    long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {  // n % 4 == 0 and out aligned: 16-byte partial loads
+        for (long long i = i0; i < n / 4; i += step) {
+            float4 acc = reinterpret_cast<const float4 *>(part)[i];
+            for (int k = 1; k < ksplit; ++k) {
+                const float4 v = reinterpret_cast<const float4 *>(part + k * stride)[i];
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            const float r[4] = {acc.x, acc.y, acc.z, acc.w};
+            store4<TOut>(out + 4 * i, r, 4, true);
+        }
+        return;
+    }
+    for (long long i = i0; i < n; i += step) {
+        float acc = part[i];
+        for (int k = 1; k < ksplit; ++k) acc += part[k * stride + i];
+        out[i] = from_f32<TOut>(acc);
+    }
+}
+
+// Split-K for GEMMs with at most half as many output tiles as SMs and a long K
+// (each tile alone on an SM leaves most SMs idle while it runs its K loop): the
+// K-blocks are cut into `ksplit` ranges of at least 16 blocks, every (tile, range)
+// unit writes an FP32 partial tile into a workspace owned by the compiled kernel,
+// and a second kernel sums the partials in range order (the result is
+// deterministic) and rounds once to the output type. Shorter ranges do not pay:
+// a unit's fixed cost (pipeline fill, the 128 KB FP32 partial tile it writes, its
+// share of the reduction) outweighs its MMAs (1024^3 BF16 with 4 ranges of 4
+// blocks: 19.3 us against 17.5 us unsplit). 1 = no split. JADE_GEMM_SPLIT_K
+// overrides the choice (read when a kernel is compiled).
+int splitk_factor(Context *ctx, const Spec &s, int kEB) {
+    const int sms = s.sm_limit ? std::min<int>((int)s.sm_limit, ctx->sm_count) : ctx->sm_count;
+    const long long tiles = (long long)((s.m + BM - 1) / BM) * (long long)((s.n + BN - 1) / BN);
+    const int kblocks = (int)((s.k + (128 / kEB) - 1) / (128 / kEB));
+    int ks = 1;
+    if (const char *force = std::getenv("JADE_GEMM_SPLIT_K"); force && *force) ks = std::atoi(force);
+    else if (tiles * 2 <= sms) ks = (int)std::min<long long>(std::min<long long>(sms / tiles, kblocks / 16), 16);
+    ks = std::max(1, std::min(ks, kblocks));
+    const int per = (kblocks + ks - 1) / ks;
+    return (kblocks + per - 1) / per;  // every range non-empty
+}
+
+template <int kEB, uint32_t kFmt, bool kBmn, typename TOut>
+LaunchFn splitk_launch(Context *ctx, const Spec &s, int ksplit) {
+    LaunchFn gemm = tc_launch<kEB, kFmt, kBmn, float, kEpiNone, false>(ctx, s, ksplit);
+    auto ws = std::make_shared<Workspace>();
+    ws->device = ctx->device;
+    const long long n = (long long)s.m * s.n;
+    if (cudaMalloc(&ws->ptr, (size_t)ksplit * n * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        throw IrError("cannot allocate the split-K workspace");
+    }
+    const int blocks = (int)std::max<long long>(1, std::min<long long>((n / 4 + 255) / 256, 8ll * ctx->sm_count));
+    return [=](cudaStream_t st, void **b) {
+        void *nb[3] = {b[0], b[1], ws->ptr};
+        cudaError_t e = gemm(st, nb);
+        if (e != cudaSuccess) return e;
+        const bool vec = n % 4 == 0 && reinterpret_cast<uintptr_t>(b[2]) % (4 * sizeof(TOut)) == 0;
+        splitk_reduce<TOut><<<blocks, 256, 0, st>>>(static_cast<const float *>(ws->ptr), static_cast<TOut *>(b[2]), n, ksplit, n, vec);
+        return cudaGetLastError();
+    };
+}
+
 template <int kEB, uint32_t kFmt, typename TOut, typename T16>
 LaunchFn pick_epilogue(Context *ctx, const Spec &s) {
     if (s.epilogue == "scatter") {
@@ -547,6 +638,10 @@ LaunchFn pick_epilogue(Context *ctx, const Spec &s) {
             return tc_launch<kEB, kFmt, false, TOut, kEpiResidual, false>(ctx, s);
         }
         return tc_launch<kEB, kFmt, true, TOut, kEpiResidual, false>(ctx, s);
+    }
+    if (!s.row_scale) {
+        if (const int ks = splitk_factor(ctx, s, kEB); ks > 1)
+            return s.b_nk ? splitk_launch<kEB, kFmt, false, TOut>(ctx, s, ks) : splitk_launch<kEB, kFmt, true, TOut>(ctx, s, ks);
     }
     if (s.b_nk) {
         if (s.row_scale) return tc_launch<kEB, kFmt, false, TOut, kEpiNone, true>(ctx, s);
@@ -578,18 +673,6 @@ __global__ void transpose_f32(const float *__restrict__ in, float *__restrict__ 
 }
 inline dim3 transpose_grid(int rows, int cols) { return dim3((cols + 31) / 32, std::min((rows + 31) / 32, 65535)); }
 
-// Device workspace owned by a compiled kernel, released with it.
-struct Workspace {
-    void *ptr = nullptr;
-    int device = 0;
-    ~Workspace() {
-        if (ptr) {
-            cudaSetDevice(device);
-            cudaFree(ptr);
-        }
-    }
-};
-
 }  // namespace
 
 bool gemm_tc_supports(const Spec &s, std::string &why) {
@@ -606,6 +689,8 @@ LaunchFn make_gemm_tc(Context *ctx, const Spec &s, std::string &impl) {
     if (!gemm_tc_supports(s, why)) throw IrError(why);
     impl = std::string("gemm_tcgen05_128x256_") + dtype_name(s.dtype) + (s.b_nk ? "_nk" : "_kn") + "_out_" + dtype_name(s.out_dtype) +
            (s.epilogue != "none" ? "_" + s.epilogue : std::string()) + (s.row_scale ? "_rowscale" : "");
+    if (s.epilogue == "none" && !s.row_scale)
+        if (const int ks = splitk_factor(ctx, s, (int)dtype_size(s.dtype)); ks > 1) impl += "_splitk" + std::to_string(ks);
     switch (s.dtype) {
         case DType::TF32:
             if (!s.b_nk) {
@@ -733,6 +818,9 @@ extern "C" JR_API int jr_gemm_tf32_kn_noalloc(const float *a, const float *b, fl
     args.tiles_n = (int)((n + BN - 1) / BN);
     args.num_tiles = args.tiles_m * args.tiles_n;
     args.kblocks = (int)((k + 31) / 32);
+    args.ksplit = 1;
+    args.kb_per = args.kblocks;
+    args.num_units = args.num_tiles;
     args.group_m = 8;
     args.err = d->err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -183,3 +183,44 @@ def test_tc_gemm_baseline_sizes_sampled(rt, dtype, b_nk, out_dtype, size):
           f"max err/tolerance = {v.max_scaled_error:.3f}")
     for x in (a, b, out):
         x.free()
+
+
+# Split-K: GEMMs with few output tiles and a long K cut K into ranges; each
+# (tile, range) writes an FP32 partial and a second kernel sums the partials in
+# range order and rounds once. Forced to 4 ranges here (JADE_GEMM_SPLIT_K) so the
+# mechanics are covered on short K too. Shapes: several tiles (1024^3), one ragged
+# tile with a partial last K block, a tall-K column strip, a single output row.
+@pytest.mark.parametrize("dtype,out_dtype", [("bf16", "bf16"), ("bf16", "fp32"), ("fp16", "fp16"), ("tf32", "fp32")])
+@pytest.mark.parametrize("m,n,k,b_nk", [(1024, 1024, 1024, False), (100, 200, 1000, True), (256, 136, 4096, True),
+                                        (1, 8, 2048, False)], ids=str)
+def test_tc_gemm_split_k(rt, monkeypatch, dtype, out_dtype, m, n, k, b_nk):
+    a, b, af, bf = operands(rt, m, n, k, dtype, b_nk, seed=k + n)
+    out = rt.alloc(m * n, out_dtype)
+    monkeypatch.setenv("JADE_GEMM_SPLIT_K", "4")
+    kern = rt.compile({"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": dtype, "out_dtype": out_dtype,
+                       "b_layout": "nk" if b_nk else "kn"})
+    assert kern.info["path"] == "tcgen05" and "_splitk4" in kern.info["impl"], kern.info
+    rt.execute([(kern, [a, b, out])], repeats=2)
+    if out_dtype == "fp32":
+        rc, v = O.validation_check(m, n, k, af, bf, rt.download(out), budget=1 << 14, fp16=(dtype == "tf32"))
+        assert rc == 0, (rc, v.first_bad_index, v.max_scaled_error, kern.info["impl"])
+    else:
+        exp = O.gemm_reference(m, n, k, af, bf)
+        rc, r = O.compare(rt.download_f32(out), exp, 2e-3 * np.abs(exp).max(), 2 ** -8)
+        assert rc == 0, r.max_abs_error
+
+
+def test_tc_gemm_split_k_deterministic_and_matches_unsplit(rt, monkeypatch):
+    m, n, k = 512, 512, 4096  # 8 tiles, 64 K-blocks: the default choice splits
+    a, b, af, bf = operands(rt, m, n, k, "bf16", False, seed=12)
+    spec = {"op": "gemm", "m": m, "n": n, "k": k, "tiled": True, "dtype": "bf16"}
+    split = rt.compile(spec)
+    assert rt.compile(dict(spec, k=1024)).info["impl"].find("_splitk") < 0  # 16 K-blocks: too short to split
+    monkeypatch.setenv("JADE_GEMM_SPLIT_K", "1")
+    whole = rt.compile(spec)
+    assert "_splitk" in split.info["impl"] and "_splitk" not in whole.info["impl"]
+    o1, o2, o3 = rt.alloc(m * n), rt.alloc(m * n), rt.alloc(m * n)
+    rt.execute([(split, [a, b, o1]), (split, [a, b, o2]), (whole, [a, b, o3])], repeats=2)
+    assert np.array_equal(rt.download(o1), rt.download(o2))
+    # the two summation orders differ only by FP32 rounding
+    np.testing.assert_allclose(rt.download(o1), rt.download(o3), rtol=0, atol=1e-3)
