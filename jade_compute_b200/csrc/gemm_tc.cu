@@ -563,6 +563,7 @@ __global__ void splitk_reduce(const float *__restrict__ part, TOut *__restrict__
     if (vec) {  // n % 4 == 0 and out aligned: 16-byte partial loads
         for (long long i = i0; i < n / 4; i += step) {
             float4 acc = reinterpret_cast<const float4 *>(part)[i];
+#pragma unroll 4
             for (int k = 1; k < ksplit; ++k) {
                 const float4 v = reinterpret_cast<const float4 *>(part + k * stride)[i];
                 acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
@@ -581,13 +582,14 @@ __global__ void splitk_reduce(const float *__restrict__ part, TOut *__restrict__
 
 // Split-K for GEMMs with at most half as many output tiles as SMs and a long K
 // (each tile alone on an SM leaves most SMs idle while it runs its K loop): the
-// K-blocks are cut into `ksplit` ranges of at least 16 blocks, every (tile, range)
+// K-blocks are cut into `ksplit` ranges of at least 32 blocks, every (tile, range)
 // unit writes an FP32 partial tile into a workspace owned by the compiled kernel,
 // and a second kernel sums the partials in range order (the result is
 // deterministic) and rounds once to the output type. Shorter ranges do not pay:
 // a unit's fixed cost (pipeline fill, the 128 KB FP32 partial tile it writes, its
 // share of the reduction) outweighs its MMAs (1024^3 BF16 with 4 ranges of 4
-// blocks: 19.3 us against 17.5 us unsplit). 1 = no split. JADE_GEMM_SPLIT_K
+// blocks: 19.3 us against 17.5 us unsplit; TF32 with 2 ranges of 16 blocks: 1.4%
+// slower). 1 = no split. JADE_GEMM_SPLIT_K
 // overrides the choice (read when a kernel is compiled).
 int splitk_factor(Context *ctx, const Spec &s, int kEB) {
     const int sms = s.sm_limit ? std::min<int>((int)s.sm_limit, ctx->sm_count) : ctx->sm_count;
@@ -595,7 +597,7 @@ int splitk_factor(Context *ctx, const Spec &s, int kEB) {
     const int kblocks = (int)((s.k + (128 / kEB) - 1) / (128 / kEB));
     int ks = 1;
     if (const char *force = std::getenv("JADE_GEMM_SPLIT_K"); force && *force) ks = std::atoi(force);
-    else if (tiles * 2 <= sms) ks = (int)std::min<long long>(std::min<long long>(sms / tiles, kblocks / 16), 16);
+    else if (tiles * 2 <= sms) ks = (int)std::min<long long>(std::min<long long>(sms / tiles, kblocks / 32), 16);
     ks = std::max(1, std::min(ks, kblocks));
     const int per = (kblocks + ks - 1) / ks;
     return (kblocks + per - 1) / per;  // every range non-empty

@@ -7,7 +7,10 @@ acceptable); its scratch is a static 16 MiB array inside the library. This test
 calls it through the C ABI twice in a row and checks each result against the
 compiled entry point (jr_compile + jr_execute2 of the same GEMM spec), within
 this suite's TF32 tolerance (src/validation.rs:35-91 form, reduced-precision
-coefficient 0.0012). The file name makes pytest collect it last.
+coefficient 0.0012). The compiled GEMM is built with split-K off
+(JADE_GEMM_SPLIT_K=1), so that both entry points sum each output's K products
+in the same order, as this entry point always does. The file name makes pytest
+collect it last.
 """
 import ctypes
 
@@ -37,7 +40,8 @@ def operands(rt, m, n, k, seed):
     return a, b
 
 
-def test_noalloc_matches_compiled_entry_point_twice():
+def test_noalloc_matches_compiled_entry_point_twice(monkeypatch):
+    monkeypatch.setenv("JADE_GEMM_SPLIT_K", "1")  # one K range, as in this entry point
     f = noalloc_fn()
     rt = jc.Runtime(0)
     try:
