@@ -54,6 +54,16 @@ MLP_COMM = ["auto"]
 B, H, S, D = 4, 16, 2048, 128
 
 
+def headline_config(world):
+    """The headline workload as both arms print it: this
+    repository's kernels and the reference arm (--impl reference) time the same
+    configuration."""
+    return {"workload": f"causal attention B={B} H={H} S={S} D={D} BF16, O BF16 (BASELINE configs[1])",
+            "global_batch": B * world, "seq_len": S, "heads": H, "head_dim": D,
+            "parallelism": f"batch x head shards over {world} GPU(s), no collective",
+            "l2": "flushed between steps (256 MiB write)", "flops_per_step_per_gpu": causal_flops(B, H, S, D)}
+
+
 def causal_flops(b, h, s, d):
     # exact kept (query, key) pairs: s(s+1)/2 per head; QK^T and PV are 2*d each
     return 2.0 * b * h * s * (s + 1) * d
@@ -198,8 +208,8 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / max(args.steps, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": f"causal attention B={B} H={H} S={S} D={D} (BASELINE configs[1]), CPU oracle port",
-                       "global_batch": B, "seq_len": S, "parallelism": "host threads"},
+            "config": headline_config(args.gpus),
+            "host_work": "FP64 oracle port of the reference's attention (materialized causal rows) on host threads",
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": descs[0]},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit_line(line)
@@ -754,11 +764,8 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (counter-based N(0,1), BF16)",
-            "config": {"workload": f"causal attention B={B} H={H} S={S} D={D} BF16, O BF16 (BASELINE configs[1])",
-                       "global_batch": B * world, "seq_len": S, "heads": H, "head_dim": D,
-                       "parallelism": f"batch x head shards over {world} GPU(s), no collective",
-                       "l2": "flushed between steps (256 MiB write)", "flops_per_step_per_gpu": flops,
-                       "kernel": attn.info.get("impl")},
+            "config": headline_config(world),
+            "kernel": attn.info.get("impl"),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
                          "frac": achieved / peaks["bf16"], "peak_source": peaks["source"] + " burst bf16",
                          "traffic": traffic},
